@@ -1,0 +1,401 @@
+"""Benchmark of the B200 BLAS core (one JSON line on rank 0).
+
+Headline workload: fp32 SGEMM 4096 x 4096 x 4096,
+transA = transB = N (the PyTorch ``a @ b`` path), column-major, alpha = 1,
+beta = 0, A and B ~ N(0, 1) from a fixed seed, issued through the public
+hipBLAS ABI (``hipblasSgemm`` of libvkblas_hipblas.so) on device-resident
+buffers.  One step = one 4096^3 GEMM per GPU.  With N GPUs the job is a
+strided-batched SGEMM of N such GEMMs sharded by batch (one per rank, no
+data-path collective): weak scaling, value = total useful FLOP/s of all ranks.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+``--impl reference`` times the reference's own CPU GEMM (``ref_gemm`` of
+test/test_gemm.c, compiled from the reference sources into oracle/_ref; the
+oracle's port of it when that build is absent) on the host cores, on a
+bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MNK = 4096
+FLOP_PER_GEMM = 2.0 * MNK ** 3
+METRIC = "SGEMM/HGEMM TFLOPS at 4096^3 (% of peak); decode GEMV HBM GB/s"
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = [("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown")]
+
+    def __init__(self, index: int, period_s: float = 0.02):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self._nv = nv
+            self._h = nv.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            pass
+        self._period = period_s
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, const in self.REASONS:
+                    if r & getattr(nv, const, 0):
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._ok:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._ok:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------- CPU reference arm
+class CpuReference:
+    """Reference ref_gemm (test/test_gemm.c:32-58) on all host threads, row-sampled.
+
+    A 4096^3 NN problem; R rows of C are computed (the reference's own
+    row-sampling idea, test/test_gemm.c:36-43), split over all host threads;
+    FLOP/s = 2*R*n*k / wall time."""
+
+    def __init__(self):
+        import numpy as np
+        from oracle import oracle as orc
+        self.np = np
+        self.threads = os.cpu_count() or 1
+        rng = np.random.default_rng(0)
+        self.A = rng.standard_normal(MNK * MNK, dtype=np.float32)
+        self.B = rng.standard_normal(MNK * MNK, dtype=np.float32)
+        self.C = np.zeros(MNK * MNK, np.float32)
+        if orc.ref is not None:
+            self.fn, self.kind = orc.ref.vkref_ref_gemm_rows_mt, "reference"
+        else:
+            self.fn, self.kind = orc.lib.orc_sgemm_colmajor_rows_mt, "port"
+        self.t_row = None
+
+    def _rows(self, rows):
+        t0 = time.perf_counter()
+        self.fn(0, 0, MNK, MNK, MNK, 1.0, self.A, MNK, self.B, MNK, 0.0, self.C, MNK, 0, rows,
+                self.threads)
+        return time.perf_counter() - t0
+
+    def sample(self, target_s: float):
+        if self.t_row is None:   # one row per thread calibrates the per-row cost
+            self.t_row = self._rows(min(MNK, self.threads))
+        per_thread = max(1, min(MNK // self.threads, int(target_s / max(self.t_row, 1e-6))))
+        rows = min(MNK, per_thread * self.threads)
+        dt = self._rows(rows)
+        tf = 2.0 * rows * MNK * MNK / dt / 1e12
+        return tf, {"kind": self.kind, "cores": self.threads,
+                    "sample": f"{rows} of 4096 rows of the 4096^3 NN SGEMM (ref_gemm, double "
+                              f"accumulation), {dt:.2f} s wall on {self.threads} threads"}
+
+
+# ------------------------------------------------------------ GPU pieces
+def _hip_sgemm(vk, hb, h, dA, dB, dC, al, be):
+    return vk.lib.hipblasSgemm(h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, MNK, MNK, MNK, al,
+                               dA.data_ptr(), MNK, dB.data_ptr(), MNK, be, dC.data_ptr(), MNK)
+
+
+def _time_loop(fn, iters, stream):
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(iters):
+        fn(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def secondary_results(vk, hb, torch, peaks):
+    """Other BASELINE configs on one GPU (device-resident inputs, CUDA events)."""
+    out = {}
+    s = torch.cuda.current_stream()
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    with hb.Handle() as h:
+        h.set_stream(s)
+        # config 3: HGEMM T/N 4096^3 and 8192^3
+        for n in (4096, 8192):
+            sets = [((torch.randn(n, n, device="cuda", generator=g) * 0.02).half(),
+                     (torch.randn(n, n, device="cuda", generator=g) * 0.02).half(),
+                     torch.empty(n, n, device="cuda", dtype=torch.float16)) for _ in range(2)]
+
+            def run(i, sets=sets, n=n):
+                A, B, C = sets[i % 2]
+                vk.lib.hipblasGemmEx_v2(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, n, n, n, al,
+                                        A.data_ptr(), vk.HIP_R_16F, n, B.data_ptr(), vk.HIP_R_16F,
+                                        n, be, C.data_ptr(), vk.HIP_R_16F, n,
+                                        vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+            for i in range(3):
+                run(i)
+            ms = _time_loop(run, 10 if n == 4096 else 4, s)
+            tf = 2.0 * n ** 3 / ms / 1e9
+            out[f"hgemm_tn_{n}"] = {"tflops": round(tf, 2), "ms": round(ms, 4),
+                                    "path": vk.PATH_NAMES[vk.last_path()],
+                                    "frac_of_bf16_burst": round(tf / peaks["bf16_tflops"], 4)}
+            del sets
+        # config 4: decode GEMV, 4 rotating weight sets (470 MB > L2)
+        K, O = 4096, 14336
+        Ws = [(torch.randn(O, K, device="cuda", generator=g) * 0.02).half() for _ in range(4)]
+        for M in (1, 4, 16):
+            X = torch.randn(M, K, device="cuda", generator=g).half()
+            C = torch.empty(M, O, device="cuda", dtype=torch.float16)
+
+            def run(i, M=M, X=X, C=C):
+                vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,
+                                     Ws[i % 4].data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
+                                     vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F, O,
+                                     vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+            for i in range(4):
+                run(i)
+            ms = _time_loop(run, 40, s)
+            nbytes = 2.0 * (O * K + M * K + M * O)
+            gbs = nbytes / ms / 1e6
+            out[f"gemv_m{M}"] = {"gbs": round(gbs, 1), "us": round(ms * 1e3, 2),
+                                 "path": vk.PATH_NAMES[vk.last_path()],
+                                 "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4)}
+        del Ws
+        # config 5: strided-batched 256 x 2048^3 NN
+        b, n = 256, 2048
+        A = (torch.randn(b, n, n, device="cuda", generator=g) * 0.02).half()
+        B = (torch.randn(b, n, n, device="cuda", generator=g) * 0.02).half()
+        C = torch.empty(b, n, n, device="cuda", dtype=torch.float16)
+
+        def run(i):
+            vk.lib.hipblasGemmStridedBatchedEx_v2(
+                h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, n, n, n, al, A.data_ptr(), vk.HIP_R_16F, n,
+                n * n, B.data_ptr(), vk.HIP_R_16F, n, n * n, be, C.data_ptr(), vk.HIP_R_16F, n,
+                n * n, b, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+        run(0)
+        ms = _time_loop(run, 3, s)
+        tf = 256 * 2.0 * n ** 3 / ms / 1e9
+        out["hgemm_batched_256x2048"] = {"tflops": round(tf, 2), "ms": round(ms, 3),
+                                         "path": vk.PATH_NAMES[vk.last_path()],
+                                         "frac_of_bf16_burst": round(tf / peaks["bf16_tflops"], 4)}
+        del A, B, C
+    return out
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        ref = CpuReference()
+        tfs = []
+        for _ in range(args.warmup):
+            ref.sample(0.2)
+        info = None
+        per_step = max(0.2, 60.0 / max(1, args.steps))
+        for _ in range(args.steps):
+            tf, info = ref.sample(per_step)
+            tfs.append(tf)
+        v = statistics.median(tfs)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOPS",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "sgemm_nn_4096^3 (ref_gemm row sample)"},
+            "cpu_baseline": dict(value=v, unit="TFLOPS", **info),
+            "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return 0
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import vkblas_b200 as vk
+    from vkblas_b200 import hipblas as hb
+    peaks, peaks_kind = _peaks()
+
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    # Two rotating buffer sets: 2 x 192 MB working set > 126 MB L2.
+    sets = [(torch.randn(MNK * MNK, device="cuda", generator=g),
+             torch.randn(MNK * MNK, device="cuda", generator=g),
+             torch.empty(MNK * MNK, device="cuda")) for _ in range(2)]
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    h = hb.Handle()
+    h.set_stream(stream)
+
+    def step(i):
+        A, B, C = sets[i % 2]
+        st = _hip_sgemm(vk, hb, h, A, B, C, al, be)
+        if st != 0:
+            raise RuntimeError(f"hipblasSgemm status {st}")
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    path = vk.PATH_NAMES[vk.last_path()]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = vk.launch_count()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches = vk.launch_count() - l0
+    ms_total = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms_total], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = world * FLOP_PER_GEMM * args.steps / (ms_total / 1e3) / 1e12
+    kernel_tflops = FLOP_PER_GEMM / (ms_step / 1e3) / 1e12
+
+    # e2e through the public ABI with host buffers: pinned H2D of A and B, the
+    # call, D2H of C -- all inside the timed region.
+    hA = torch.randn(MNK * MNK, generator=torch.Generator().manual_seed(7)).pin_memory()
+    hB = torch.randn(MNK * MNK, generator=torch.Generator().manual_seed(8)).pin_memory()
+    hC = torch.empty(MNK * MNK).pin_memory()
+    dA, dB, dC = sets[0]
+
+    def e2e_step(i):
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        st = _hip_sgemm(vk, hb, h, dA, dB, dC, al, be)
+        if st != 0:
+            raise RuntimeError(f"hipblasSgemm status {st}")
+        hC.copy_(dC, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for i in range(2):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    e2e_ms = _time_loop(e2e_step, e2e_steps, stream)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = world * FLOP_PER_GEMM / (e2e_ms / 1e3) / 1e12
+
+    if path == "tc":
+        kernel_name = "3xTF32 tcgen05 SGEMM"
+        peak = peaks["bf16_tflops"] / 2.0 / 3.0
+        peak_note = (f"{peaks_kind} bf16 burst {peaks['bf16_tflops']} TF / 2 (TF32 rate) / 3 "
+                     "(three TF32 MMAs per useful FLOP)")
+    else:
+        kernel_name = "FFMA SIMT SGEMM"
+        peak = 148 * 128 * 2 * (peaks.get("sm_max_mhz", 1965.0) * 1e6) / 1e12
+        peak_note = "FP32 SIMT nominal: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
+    roof = {"bound": "tensor", "kernel": kernel_name, "achieved": round(kernel_tflops, 2),
+            "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4),
+            "peak_source": peak_note, "traffic": None}
+
+    result = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (A,B ~ N(0,1) fp32, seeded per rank)",
+        "config": {"workload": "sgemm_nn_4096^3: hipblasSgemm(N, N, 4096, 4096, 4096), "
+                               "column-major, alpha=1 beta=0 (BASELINE config 2)",
+                   "per_gpu": "one 4096^3 GEMM per step (strided-batched SGEMM sharded by batch)",
+                   "parallelism": f"batch-shard x{world}", "path": path,
+                   "l2": "2 rotating A/B/C sets (384 MB working set > 126 MB L2)"},
+        "roofline": roof,
+        "e2e": {"value": round(e2e_val, 3), "unit": "TFLOPS",
+                "h2d_bytes_per_step": 2 * MNK * MNK * 4, "d2h_bytes_per_step": MNK * MNK * 4},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    del sets, hA, hB, hC
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, info = CpuReference().sample(8.0)
+        result["cpu_baseline"] = dict(value=tf, unit="TFLOPS", **info)
+    if rank == 0 and world == 1 and not args.no_secondary:
+        try:
+            result["secondary"] = secondary_results(vk, hb, torch, peaks)
+        except Exception as exc:   # secondary numbers never hide the headline
+            result["secondary"] = {"error": repr(exc)}
+    h.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,73 @@
+/* vkblas_b200.h -- B200-specific extensions of the vkblas C API.
+ *
+ * These entry points have no counterpart in the reference's vkblas.h (its
+ * engine was synchronous, single-stream and single-device).  They expose what
+ * a stream-ordered CUDA library needs: a stream per calling thread, device
+ * resident alpha/beta, kernel-path control for tests and benchmarks, the
+ * device status word of the bounded waits, and the multi-GPU shard planner.
+ */
+#pragma once
+#include "vkblas.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum { VKBLAS_DT_F32 = 0, VKBLAS_DT_F16 = 1, VKBLAS_DT_BF16 = 2 } vkblas_dtype_t;
+
+/* Kernel families.  AUTO lets the dispatcher choose. */
+typedef enum {
+    VKBLAS_PATH_AUTO = 0,
+    VKBLAS_PATH_SIMT = 1,   /* exact SIMT GEMM: sequential fp32 fmaf per output      */
+    VKBLAS_PATH_TC = 2,     /* tcgen05 GEMM: kind::f16 (fp16/bf16) or 3xTF32 (fp32)   */
+    VKBLAS_PATH_GEMV = 3    /* split-K decode GEMV (M <= 16, op_b == T, 2-byte types) */
+} vkblas_path_t;
+
+/* Generic entry used by the hipBLAS shim.  alpha and beta point to fp32
+ * scalars in host memory (scalars_on_device == 0) or device memory (1); in
+ * the device case the kernels read them, nothing is copied to the host.
+ * stream: a cudaStream_t (NULL = legacy default stream). */
+vkblas_status_t vkblas_gemm_ex(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op_t op_b,
+                               uint32_t M, uint32_t N, uint32_t K,
+                               const float* alpha, const float* beta, int scalars_on_device,
+                               const void* A, uint32_t lda, const void* B, uint32_t ldb,
+                               void* C, uint32_t ldc, uint32_t batch,
+                               int64_t stride_a, int64_t stride_b, int64_t stride_c,
+                               void* stream);
+
+/* Stream used by the vkblas_gemm_* calls made from the calling thread
+ * (thread-local; default NULL = legacy default stream). */
+void vkblas_set_stream(void* stream);
+void* vkblas_get_stream(void);
+
+/* Thread-local kernel-path override (VKBLAS_PATH_AUTO by default).  A forced
+ * path that cannot run the call (alignment, shape) makes the call return
+ * VKBLAS_ERR_FALLBACK instead of silently taking another path. */
+void vkblas_b200_set_path(int path);
+int vkblas_b200_get_path(void);
+/* Path taken by the last successful call on this thread (vkblas_path_t). */
+int vkblas_b200_last_path(void);
+/* Thread-local split-K factor for the GEMV path: 0 = automatic, else 1..16. */
+void vkblas_b200_set_splitk(int splitk);
+
+/* Device status word written by kernels whose bounded waits ran out (0 = no
+ * error).  Synchronises the current device first.  clear != 0 resets it. */
+int vkblas_b200_device_status(int clear);
+
+/* Number of kernels this library launched from the calling process (all
+ * threads); used by tests and benchmarks to prove the native path ran. */
+uint64_t vkblas_b200_launch_count(void);
+
+/* Library version string. */
+const char* vkblas_b200_version(void);
+
+/* Multi-GPU shard planner (pure host logic).  Splits `units` work units
+ * (batch entries, or column blocks of `block` columns) into `world` contiguous
+ * ranges as evenly as possible; returns this rank's [begin, begin+count).
+ * Returns VKBLAS_ERR_PARAM for world < 1 or rank outside [0, world). */
+vkblas_status_t vkblas_shard_range(uint64_t units, uint64_t block, int rank, int world,
+                                   uint64_t* begin, uint64_t* count);
+
+#ifdef __cplusplus
+}
+#endif

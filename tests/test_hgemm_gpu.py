@@ -1,0 +1,282 @@
+"""fp16 / bf16 GEMM and decode-GEMV parity on a B200.
+
+* test/test_h.c:89-226 cases through ``vkblas_gemm_f16`` / ``vkblas_gemm_bf16``
+  (engine API): reference bar max |diff| < 0.05 against the reference
+  ``cpu_ref`` output (golden-pinned oracle); the exact SIMT path additionally
+  bit-identical to the sequential-fmaf oracle.
+* test/test_v9h.c:63-71 cases through ``hipblasGemmEx`` (legacy types):
+  reference bar rel <= 0.02 (test/test_v9h.c:305-312).
+* BASELINE config 3 (M=N=K in {4096, 8192, 16384}, hipBLAS T/N) and config 5
+  (strided-batched 256 x 2048^3 NN): relative error <= 2e-3 on sampled rows.
+* BASELINE config 4 decode GEMV (M in {1,4,16}, K=4096, N=14336, split-K in
+  {1,4,8}) through ``hipblasGemmEx`` exactly as test/bench_decode.c:52-64 calls
+  it: relative Frobenius error <= 2e-3 against a double-precision product.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import ref_cases as rc
+
+pytestmark = pytest.mark.gpu
+
+import vkblas_b200 as vk  # noqa: E402
+from vkblas_b200 import hipblas as hb  # noqa: E402
+from oracle import oracle as orc  # noqa: E402
+from gpu_util import dev_u16, host_u16, check_status  # noqa: E402
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+H_ALL = [("single", c) for c in rc.TEST_H_CASES] + [("batch", c) for c in rc.TEST_H_BATCH_CASES]
+
+
+@pytest.fixture(scope="module")
+def gold_h():
+    return dict(np.load(os.path.join(GOLD, "ref_test_h.npz")))
+
+
+@pytest.mark.parametrize("path", ["simt", "auto"])
+@pytest.mark.parametrize("idx", range(len(H_ALL)))
+def test_engine_half_reference_cases(idx, path, cuda, gold_h):
+    import torch
+    kind, c = H_ALL[idx]
+    dt = c["dtype"]
+    A, B, C0 = orc.gen_test_h(c["seed"], dt, c["na"], c["nb"], c["nc"], kind == "batch")
+    R = C0.copy()   # reference cpu_ref output, through the golden-pinned oracle
+    orc.hgemm_rowmajor(dt, 2, c["op_a"], c["op_b"], c["M"], c["N"], c["K"], c["alpha"], A, c["lda"],
+                       B, c["ldb"], c["beta"], R, c["ldc"], c.get("batch", 1), c.get("sa", 0),
+                       c.get("sb", 0), c.get("sc", 0))
+    if f"h{idx:03d}_R" in gold_h:
+        np.testing.assert_array_equal(R, gold_h[f"h{idx:03d}_R"])
+    dA, dB, dC = dev_u16(A, dt), dev_u16(B, dt), dev_u16(C0, dt)
+    vk.set_path(vk.PATH_SIMT if path == "simt" else vk.PATH_AUTO)
+    try:
+        vk.set_stream(torch.cuda.current_stream())
+        st = vk.gemm(vk.DT_BF16 if dt else vk.DT_F16, c["op_a"], c["op_b"], c["M"], c["N"], c["K"],
+                     c["alpha"], dA.data_ptr(), c["lda"], dB.data_ptr(), c["ldb"], c["beta"],
+                     dC.data_ptr(), c["ldc"], c.get("batch", 1), c.get("sa", 0), c.get("sb", 0),
+                     c.get("sc", 0))
+        torch.cuda.synchronize()
+    finally:
+        vk.set_path(vk.PATH_AUTO)
+    assert st == vk.VKBLAS_OK
+    check_status()
+    got = host_u16(dC)
+    g = orc.widen(dt, got).astype(np.float64)
+    w = orc.widen(dt, R).astype(np.float64)
+    assert np.max(np.abs(g - w)) < 0.05, "reference bar (test/test_h.c:141)"
+    if vk.last_path() == vk.PATH_SIMT:
+        ref = C0.copy()
+        orc.hgemm_rowmajor(dt, 1, c["op_a"], c["op_b"], c["M"], c["N"], c["K"], c["alpha"], A,
+                           c["lda"], B, c["ldb"], c["beta"], ref, c["ldc"], c.get("batch", 1),
+                           c.get("sa", 0), c.get("sb", 0), c.get("sc", 0))
+        np.testing.assert_array_equal(got, ref)
+
+
+def _libc_rand_half_pm(seed, n, libc):
+    """test/test_v9h.c:80-90: random sign, magnitude in [0.5, 1) as raw 2-byte patterns."""
+    out = np.empty(n, np.uint16)
+    libc.srand(seed)
+    for i in range(n):
+        v = libc.rand() % 0x0400 + 0x3800
+        if libc.rand() & 1:
+            v |= 0x8000
+        out[i] = v
+    return out
+
+
+@pytest.mark.parametrize("case", range(len(rc.TEST_V9H_CASES)))
+@pytest.mark.parametrize("dt", [0, 1])
+def test_hipblas_gemmex_v9h_cases(case, dt, cuda):
+    """test/test_v9h.c through hipblasGemmEx (HIPBLAS_R_16B / HIPBLAS_R_16F)."""
+    import torch
+    libc = ctypes.CDLL("libc.so.6")
+    M, N, K, lda, ldb, ldc, ta, tb = rc.TEST_V9H_CASES[case]
+    d = 0 if dt else 1                      # test_v9h: d=0 bf16, d=1 fp16
+    sa = (K if ta else M) * lda
+    sb = (N if tb else K) * ldb
+    libc.srand(777 + d * 100 + case)
+    A = np.empty(sa, np.uint16)
+    B = np.empty(sb, np.uint16)
+    for arr in (A, B):
+        for i in range(arr.size):
+            v = libc.rand() % 0x0400 + 0x3800
+            if libc.rand() & 1:
+                v |= 0x8000
+            arr[i] = v
+    dA, dB = dev_u16(A, dt), dev_u16(B, dt)
+    dC = dev_u16(np.zeros(M * ldc, np.uint16), dt)
+    typ = vk.HIPBLAS_R_16B if dt else vk.HIPBLAS_R_16F
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    with hb.Handle() as h:
+        st = vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T if tb else vk.HIPBLAS_OP_N,
+                                  vk.HIPBLAS_OP_T if ta else vk.HIPBLAS_OP_N, N, M, K, al,
+                                  dB.data_ptr(), typ, ldb, dA.data_ptr(), typ, lda, be,
+                                  dC.data_ptr(), typ, ldc, vk.HIPBLAS_COMPUTE_32F,
+                                  vk.HIPBLAS_GEMM_DEFAULT)
+        torch.cuda.synchronize()
+    assert st == 0
+    got = orc.widen(dt, host_u16(dC)).reshape(M, ldc)[:, :N].astype(np.float64)
+    Af = orc.widen(dt, A).astype(np.float32)
+    Bf = orc.widen(dt, B).astype(np.float32)
+    opA = (Af.reshape(K, lda)[:, :M].T if ta else Af.reshape(M, lda)[:, :K])
+    opB = (Bf.reshape(N, ldb)[:, :K].T if tb else Bf.reshape(K, ldb)[:, :N])
+    acc = opA.astype(np.float64) @ opB.astype(np.float64)
+    rel = np.abs(got - acc) / (1.0 + np.abs(acc))
+    assert rel.max() < 0.02, f"max rel {rel.max()} (reference bar 0.02)"
+
+
+def _torch_dtype(dt):
+    import torch
+    return torch.bfloat16 if dt else torch.float16
+
+
+@pytest.mark.parametrize("size", [4096, 8192, 16384])
+def test_config3_hgemm_TN(size, cuda):
+    """hipBLAS transA=T, transB=N, M=N=K, A,B ~ N(0,0.02) fp16."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(3000 + size)
+    A = (torch.randn(size, size, device="cuda", generator=g) * 0.02).half()   # hipBLAS A, lda=K (T)
+    B = (torch.randn(size, size, device="cuda", generator=g) * 0.02).half()   # hipBLAS B, ldb=K (N)
+    C = torch.empty(size, size, device="cuda", dtype=torch.float16)
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    with hb.Handle() as h:
+        h.set_stream(torch.cuda.current_stream())
+        st = vk.lib.hipblasGemmEx_v2(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, size, size, size, al,
+                                     A.data_ptr(), vk.HIP_R_16F, size, B.data_ptr(), vk.HIP_R_16F,
+                                     size, be, C.data_ptr(), vk.HIP_R_16F, size,
+                                     vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+        torch.cuda.synchronize()
+    assert st == 0
+    check_status()
+    # column-major: C[i + j*ldc] = sum_k A[k + i*lda] * B[k + j*ldb]; as torch row-major
+    # arrays: Ct[j, i] = sum_k Bt[j, k] * At[i, k]  ->  Ct = Bt @ At^T
+    cols = torch.tensor([0, 1, size // 3, size // 2 + 7, size - 2, size - 1], device="cuda")
+    want = (B[cols].double() @ A.double().T)                    # rows j of Ct
+    got = C[cols].double()
+    err = (torch.linalg.norm(got - want) / torch.linalg.norm(want)).item()
+    assert err <= 2e-3, f"relative error {err}"
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+@pytest.mark.parametrize("splitk", [1, 4, 8])
+def test_config4_decode_gemv(M, splitk, cuda):
+    """BASELINE config 4 through hipblasGemmEx(T, N, m=O, n=M, k=K) as test/bench_decode.c."""
+    import torch
+    K, O = 4096, 14336
+    g = torch.Generator(device="cuda").manual_seed(40 + M * 10 + splitk)
+    W = (torch.randn(O, K, device="cuda", generator=g) * 0.02).half()     # W: O rows x K (lda=K)
+    X = (torch.randn(M, K, device="cuda", generator=g)).half()            # X: M rows x K (ldb=K)
+    C = torch.full((M, O), float("nan"), device="cuda", dtype=torch.float16)
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    vk.set_splitk(splitk)
+    try:
+        with hb.Handle() as h:
+            h.set_stream(torch.cuda.current_stream())
+            st = vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,
+                                      W.data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
+                                      vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F, O,
+                                      vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+            torch.cuda.synchronize()
+        assert vk.last_path() == vk.PATH_GEMV
+    finally:
+        vk.set_splitk(0)
+    assert st == 0
+    check_status()
+    want = X.double() @ W.double().T
+    err = (torch.linalg.norm(C.double() - want) / torch.linalg.norm(want)).item()
+    assert err <= 2e-3, f"relative error {err}"
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("shape", [(3, 100, 72), (16, 129, 200), (9, 64, 4096), (1, 8, 8)])
+@pytest.mark.parametrize("splitk", [1, 2, 3])
+def test_gemv_edges_against_splitk_oracle(dt, shape, splitk, cuda):
+    """Ragged N, K not a multiple of the 64-wide chunk, beta != 0, bf16."""
+    import torch
+    M, N, K = shape
+    rng = np.random.default_rng(M * 1000 + N + K + dt)
+    X = orc.narrow(dt, rng.uniform(-1, 1, M * K).astype(np.float32))
+    W = orc.narrow(dt, rng.uniform(-1, 1, N * K).astype(np.float32))
+    C0 = orc.narrow(dt, rng.uniform(-1, 1, M * N).astype(np.float32))
+    dX, dW, dC = dev_u16(X, dt), dev_u16(W, dt), dev_u16(C0, dt)
+    vk.set_splitk(splitk)
+    vk.set_path(vk.PATH_GEMV)
+    try:
+        vk.set_stream(torch.cuda.current_stream())
+        st = vk.gemm(vk.DT_BF16 if dt else vk.DT_F16, 0, 1, M, N, K, 0.5, dX.data_ptr(), K,
+                     dW.data_ptr(), K, -0.75, dC.data_ptr(), N)
+        torch.cuda.synchronize()
+    finally:
+        vk.set_splitk(0)
+        vk.set_path(vk.PATH_AUTO)
+    assert st == vk.VKBLAS_OK
+    want = orc.hgemm_rowmajor_f64(dt, 0, 1, M, N, K, 0.5, X, K, W, K, -0.75, C0, N)[0]
+    got = orc.widen(dt, host_u16(dC)).reshape(M, N)
+    err = orc.rel_frobenius(got, want)
+    assert err <= (8e-3 if dt else 2e-3), err
+    # the reference's split-K model (segment partials summed in order) agrees too
+    ref = C0.copy()
+    orc.hgemm_rowmajor_splitk(dt, 0, 1, M, N, K, splitk, 0.5, X, K, W, K, -0.75, ref, N)
+    assert np.max(np.abs(got - orc.widen(dt, ref).reshape(M, N))) <= 0.02
+
+
+def test_config5_strided_batched_hgemm(cuda):
+    """256 x 2048^3 fp16 NN strided-batched, sampled check."""
+    import torch
+    b, n = 256, 2048
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = (torch.randn(b, n, n, device="cuda", generator=g) * 0.02).half()
+    B = (torch.randn(b, n, n, device="cuda", generator=g) * 0.02).half()
+    C = torch.empty(b, n, n, device="cuda", dtype=torch.float16)
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    with hb.Handle() as h:
+        h.set_stream(torch.cuda.current_stream())
+        st = vk.lib.hipblasGemmStridedBatchedEx_v2(
+            h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, n, n, n, al, A.data_ptr(), vk.HIP_R_16F, n,
+            n * n, B.data_ptr(), vk.HIP_R_16F, n, n * n, be, C.data_ptr(), vk.HIP_R_16F, n, n * n,
+            b, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+        torch.cuda.synchronize()
+    assert st == 0
+    check_status()
+    # column-major per batch: Ct[j, i] = sum_k Bt[j, k] * At[k, i]  ->  Ct = Bt @ At
+    for bi in (0, 97, 255):
+        cols = torch.tensor([0, 5, 1024, 2047], device="cuda")
+        want = B[bi][cols].double() @ A[bi].double()
+        got = C[bi][cols].double()
+        err = (torch.linalg.norm(got - want) / torch.linalg.norm(want)).item()
+        assert err <= 2e-3, (bi, err)
+
+
+def test_rocblas_gemm_ex_f16_and_inplace_rule(cuda):
+    """rocblas_gemm_ex: handled when c == d and compute f32 (src/vkblas_hipblas.c:840);
+    c != d is forwarded, i.e. not_implemented without a real rocBLAS."""
+    import torch
+    m, n, k = 64, 48, 40
+    rng = np.random.default_rng(11)
+    A = orc.f2h(rng.uniform(-1, 1, m * k).astype(np.float32))
+    B = orc.f2h(rng.uniform(-1, 1, k * n).astype(np.float32))
+    C0 = orc.f2h(rng.uniform(-1, 1, m * n).astype(np.float32))
+    dA, dB, dC = dev_u16(A, 0), dev_u16(B, 0), dev_u16(C0, 0)
+    al, be = hb.fptr(1.0), hb.fptr(0.5)
+    with hb.RocHandle() as h:
+        st = vk.lib.rocblas_gemm_ex(h.h, vk.ROCBLAS_OP_N, vk.ROCBLAS_OP_N, m, n, k, al,
+                                    dA.data_ptr(), vk.ROCBLAS_F16, m, dB.data_ptr(), vk.ROCBLAS_F16,
+                                    k, be, dC.data_ptr(), vk.ROCBLAS_F16, m, dC.data_ptr(),
+                                    vk.ROCBLAS_F16, m, vk.ROCBLAS_F32, 0, 0, 0)
+        torch.cuda.synchronize()
+        assert st == vk.rocblas_status_success
+        other = torch.empty_like(dC)
+        st2 = vk.lib.rocblas_gemm_ex(h.h, vk.ROCBLAS_OP_N, vk.ROCBLAS_OP_N, m, n, k, al,
+                                     dA.data_ptr(), vk.ROCBLAS_F16, m, dB.data_ptr(),
+                                     vk.ROCBLAS_F16, k, be, dC.data_ptr(), vk.ROCBLAS_F16, m,
+                                     other.data_ptr(), vk.ROCBLAS_F16, m, vk.ROCBLAS_F32, 0, 0, 0)
+        assert st2 == vk.rocblas_status_not_implemented
+    # column-major C(m x n) = A(m x k) B(k x n) + 0.5 C
+    Af = orc.h2f(A).reshape(k, m).T.astype(np.float64)
+    Bf = orc.h2f(B).reshape(n, k).T.astype(np.float64)
+    Cf = orc.h2f(C0).reshape(n, m).T.astype(np.float64)
+    want = Af @ Bf + 0.5 * Cf
+    got = orc.h2f(host_u16(dC)).reshape(n, m).T
+    assert np.max(np.abs(got - want)) < 0.02

@@ -1,0 +1,145 @@
+"""vkblas_b200 -- B200-native BLAS core behind the vkblas / hipBLAS C ABI.
+
+The product is the shared library ``libvkblas_hipblas.so`` built in-tree from
+``csrc/`` (see ``build.py``).  This package only loads it with ctypes and
+offers thin helpers that pass torch tensors' device pointers to the C entry
+points; no arithmetic happens in Python and there is no CPU fallback: if the
+library is missing, importing raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libvkblas_hipblas.so")
+
+VKBLAS_OK, VKBLAS_ERR_INIT, VKBLAS_ERR_IMPORT, VKBLAS_ERR_PARAM, VKBLAS_ERR_FALLBACK = range(5)
+OP_N, OP_T = 0, 1
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+PATH_AUTO, PATH_SIMT, PATH_TC, PATH_GEMV = 0, 1, 2, 3
+PATH_NAMES = {PATH_AUTO: "auto", PATH_SIMT: "simt", PATH_TC: "tc", PATH_GEMV: "gemv"}
+
+# hipBLAS / rocBLAS ABI values (include/vkblas_hipblas.h)
+HIPBLAS_OP_N, HIPBLAS_OP_T, HIPBLAS_OP_C = 111, 112, 113
+HIPBLAS_STATUS_SUCCESS, HIPBLAS_STATUS_INVALID_VALUE, HIPBLAS_STATUS_NOT_SUPPORTED = 0, 3, 7
+HIPBLAS_POINTER_MODE_HOST, HIPBLAS_POINTER_MODE_DEVICE = 0, 1
+HIP_R_32F, HIP_R_16F, HIP_R_16BF = 0, 2, 14
+HIPBLAS_R_16F, HIPBLAS_R_32F, HIPBLAS_R_16B = 150, 151, 168
+HIPBLAS_COMPUTE_32F, HIPBLAS_COMPUTE_32F_PEDANTIC = 2, 3
+HIPBLAS_GEMM_DEFAULT = 160
+ROCBLAS_OP_N, ROCBLAS_OP_T = 111, 112
+ROCBLAS_F16, ROCBLAS_F32, ROCBLAS_BF16 = 150, 151, 168
+rocblas_status_success, rocblas_status_not_implemented, rocblas_status_invalid_value = 0, 2, 11
+
+
+class VkblasError(RuntimeError):
+    pass
+
+
+def _load() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise VkblasError(
+            f"{LIB_PATH} is missing: build it with `python -m vkblas_b200.build` "
+            "(there is no CPU fallback)")
+    lib = C.CDLL(LIB_PATH)
+    u32, i64, f32, vp, i32 = C.c_uint32, C.c_int64, C.c_float, C.c_void_p, C.c_int
+    gemm_args = [i32, i32, u32, u32, u32, f32, vp, u32, vp, u32, f32, vp, u32, u32, i64, i64, i64]
+    for name in ("vkblas_gemm_f32", "vkblas_gemm_f16", "vkblas_gemm_bf16", "vkblas_gemm_bf16_hipblas"):
+        fn = getattr(lib, name)
+        fn.argtypes = gemm_args
+        fn.restype = i32
+    lib.vkblas_gemm_ex.argtypes = [i32, i32, i32, u32, u32, u32, vp, vp, i32, vp, u32, vp, u32, vp,
+                                   u32, u32, i64, i64, i64, vp]
+    lib.vkblas_gemm_ex.restype = i32
+    lib.vkblas_set_stream.argtypes = [vp]
+    lib.vkblas_get_stream.restype = vp
+    lib.vkblas_b200_set_path.argtypes = [i32]
+    lib.vkblas_b200_get_path.restype = i32
+    lib.vkblas_b200_last_path.restype = i32
+    lib.vkblas_b200_set_splitk.argtypes = [i32]
+    lib.vkblas_b200_device_status.argtypes = [i32]
+    lib.vkblas_b200_device_status.restype = i32
+    lib.vkblas_b200_launch_count.restype = C.c_uint64
+    lib.vkblas_b200_version.restype = C.c_char_p
+    lib.vkblas_cache_invalidate_base.argtypes = [vp]
+    lib.vkblas_shard_range.argtypes = [C.c_uint64, C.c_uint64, i32, i32,
+                                       C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+    lib.vkblas_shard_range.restype = i32
+    return lib
+
+
+lib = _load()
+
+
+def version() -> str:
+    return lib.vkblas_b200_version().decode()
+
+
+def set_stream(stream) -> None:
+    """Stream (cudaStream_t as int, or a torch.cuda.Stream) for this thread's calls."""
+    if stream is not None and hasattr(stream, "cuda_stream"):
+        stream = stream.cuda_stream
+    lib.vkblas_set_stream(C.c_void_p(stream or 0))
+
+
+def set_path(path: int) -> None:
+    lib.vkblas_b200_set_path(int(path))
+
+
+def last_path() -> int:
+    return lib.vkblas_b200_last_path()
+
+
+def set_splitk(s: int) -> None:
+    lib.vkblas_b200_set_splitk(int(s))
+
+
+def device_status(clear: bool = True) -> int:
+    return lib.vkblas_b200_device_status(1 if clear else 0)
+
+
+def launch_count() -> int:
+    return int(lib.vkblas_b200_launch_count())
+
+
+def shard_range(units: int, rank: int, world: int, block: int = 1):
+    b = C.c_uint64()
+    n = C.c_uint64()
+    st = lib.vkblas_shard_range(units, block, rank, world, C.byref(b), C.byref(n))
+    if st != VKBLAS_OK:
+        raise VkblasError(f"vkblas_shard_range status {st}")
+    return int(b.value), int(n.value)
+
+
+_GEMM_BY_DTYPE = {DT_F32: "vkblas_gemm_f32", DT_F16: "vkblas_gemm_f16", DT_BF16: "vkblas_gemm_bf16"}
+
+
+def gemm(dtype: int, op_a: int, op_b: int, M: int, N: int, K: int, alpha: float, A: int, lda: int,
+         B: int, ldb: int, beta: float, C_: int, ldc: int, batch: int = 1, sa: int = 0,
+         sb: int = 0, sc: int = 0) -> int:
+    """Row-major engine call (reference src/vkblas.h:19-36) on raw device pointers.
+
+    Returns the vkblas_status_t value."""
+    fn = getattr(lib, _GEMM_BY_DTYPE[dtype])
+    return fn(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C_, ldc, batch, sa, sb, sc)
+
+
+def dtype_of(t) -> int:
+    import torch
+    return {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}[t.dtype]
+
+
+def gemm_tensors(op_a: int, op_b: int, M: int, N: int, K: int, alpha: float, A, lda: int, B,
+                 ldb: int, beta: float, Cout, ldc: int, batch: int = 1, sa: int = 0, sb: int = 0,
+                 sc: int = 0, stream=None) -> None:
+    """Engine call on torch CUDA tensors (flat storage, element strides), on
+    ``stream`` (default: torch's current stream).  Raises on a non-OK status."""
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    set_stream(stream)
+    st = gemm(dtype_of(A), op_a, op_b, M, N, K, alpha, A.data_ptr(), lda, B.data_ptr(), ldb, beta,
+              Cout.data_ptr(), ldc, batch, sa, sb, sc)
+    if st != VKBLAS_OK:
+        raise VkblasError(f"vkblas gemm returned status {st}")

@@ -1,0 +1,82 @@
+// common.cuh -- shared definitions of the B200 BLAS core kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace vkb {
+
+// Element types of the engine (values match vkblas_dtype_t).
+enum DType : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2 };
+
+// One GEMM call in the engine's row-major contract (reference
+// src/vkblas.h:19-26): C[M,N] = alpha*op(A)*op(B) + beta*C per batch entry.
+struct GemmProblem {
+    int dtype;
+    int op_a, op_b;                 // 0 = N, 1 = T
+    uint32_t M, N, K;
+    float alpha, beta;              // used when d_alpha / d_beta are null
+    const float* d_alpha;           // device-resident scalars (pointer mode DEVICE)
+    const float* d_beta;
+    const void* A; uint32_t lda;
+    const void* B; uint32_t ldb;
+    void* C; uint32_t ldc;
+    uint32_t batch;
+    int64_t sa, sb, sc;             // element strides between batch entries (0 = broadcast)
+};
+
+// Device status codes written by bounded waits that ran out.
+enum DeviceStatus : int {
+    DS_OK = 0,
+    DS_TIMEOUT_PRODUCER = 1,
+    DS_TIMEOUT_MMA = 2,
+    DS_TIMEOUT_EPILOGUE = 3,
+    DS_TIMEOUT_TRANSFORM = 4,
+};
+
+// Element load/store through fp32.
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float load(const float* p) { return *p; }
+    static __device__ __forceinline__ float to_f(float v) { return v; }
+    static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__half> {
+    static __device__ __forceinline__ float load(const __half* p) { return __half2float(*p); }
+    static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// The reference epilogue `alpha*acc + beta*c` (gemm_f32_64x64_tmpl.comp:158-160)
+// with both products and the sum rounded separately (no contraction), and c
+// not read when beta == 0.
+__device__ __forceinline__ float epilogue(float alpha, float acc, float beta, float c) {
+    return __fadd_rn(__fmul_rn(alpha, acc), __fmul_rn(beta, c));
+}
+
+__device__ __forceinline__ void load_scalars(const float* d_alpha, const float* d_beta,
+                                             float& alpha, float& beta) {
+    if (d_alpha) alpha = *d_alpha;
+    if (d_beta) beta = *d_beta;
+}
+
+}  // namespace vkb
+
+// Kernel launchers (host side), one per translation unit.
+namespace vkb {
+cudaError_t launch_simt_gemm(const GemmProblem& p, cudaStream_t s);
+bool gemv_supported(const GemmProblem& p);
+int gemv_auto_splitk(const GemmProblem& p, int num_sms);
+size_t gemv_workspace_bytes(const GemmProblem& p, int splitk);
+cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaStream_t s);
+bool umma_supported(const GemmProblem& p);
+cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, cudaStream_t s);
+// Host-side launch counter (all kernels of this library).
+void count_launch();
+}  // namespace vkb

@@ -1,0 +1,369 @@
+// engine.cu -- dispatcher and C API of the B200 BLAS core.
+//
+// Replaces the reference engine (lakitu12/vkblas src/vkblas.c): its Vulkan
+// instance, pipelines, dma-buf import cache (src/ic_cache.h) and global
+// submit-and-wait lock are gone.  Device pointers are used directly, work is
+// enqueued on a CUDA stream, and the only shared state is a per-device record
+// (SM count, status word) plus a grow-only workspace per (device, stream).
+//
+// Path selection (the reference's heuristics, src/vkblas.c:3104-3341 and
+// 3517-3651, re-derived for B200):
+//   1. 2-byte types, M <= 16, op_b == T, op_a == N, batch == 1 (decode
+//      shapes, the reference's matvec family)  -> split-K GEMV (gemv.cu);
+//   2. operands that satisfy TMA's alignment rules (16-byte aligned bases,
+//      leading dimensions and batch strides)       -> tcgen05 GEMM
+//      (umma_gemm.cu): kind::f16 for fp16/bf16, 3xTF32 for fp32;
+//   3. anything else                              -> exact SIMT GEMM
+//      (simt_gemm.cu), which accepts every op, ld and stride.
+// Environment overrides, read once: VKBLAS_SGEMM=ffma|3xtf32|auto,
+// VKBLAS_HGEMM=simt|tc|auto, VKBLAS_GEMV=0|1, VKBLAS_GEMV_SPLITK=n,
+// VKBLAS_TRACE=1 (one line per call on stderr).
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "vkblas_b200.h"
+
+namespace vkb {
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
+
+struct Config {
+    int sgemm = 0;      // 0 auto, 1 ffma (SIMT), 2 3xtf32 (TC)
+    int hgemm = 0;      // 0 auto, 1 simt, 2 tc
+    int gemv = 1;
+    int gemv_splitk = 0;
+    bool trace = false;
+};
+
+const Config& config() {
+    static Config c = [] {
+        Config k;
+        if (const char* e = getenv("VKBLAS_SGEMM")) {
+            if (!strcmp(e, "ffma")) k.sgemm = 1;
+            else if (!strcmp(e, "3xtf32")) k.sgemm = 2;
+        }
+        if (const char* e = getenv("VKBLAS_HGEMM")) {
+            if (!strcmp(e, "simt")) k.hgemm = 1;
+            else if (!strcmp(e, "tc")) k.hgemm = 2;
+        }
+        if (const char* e = getenv("VKBLAS_GEMV")) k.gemv = atoi(e) != 0;
+        if (const char* e = getenv("VKBLAS_GEMV_SPLITK")) k.gemv_splitk = atoi(e);
+        k.trace = getenv("VKBLAS_TRACE") != nullptr;
+        return k;
+    }();
+    return c;
+}
+
+struct Workspace {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct DeviceState {
+    int dev = -1;
+    int num_sms = 0;
+    int cc_major = 0, cc_minor = 0;
+    int* d_status = nullptr;
+    std::mutex mu;
+    std::unordered_map<cudaStream_t, Workspace> ws;
+};
+
+std::mutex g_dev_mu;
+DeviceState* g_devs[64] = {};
+
+DeviceState* device_state(int dev) {
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (g_devs[dev]) return g_devs[dev];
+    auto* d = new DeviceState();
+    d->dev = dev;
+    if (cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d->cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d->cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaMalloc(&d->d_status, sizeof(int)) != cudaSuccess ||
+        cudaMemset(d->d_status, 0, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        delete d;
+        return nullptr;
+    }
+    g_devs[dev] = d;
+    return d;
+}
+
+// Grow-only scratch per (device, stream).  Growth frees the old buffer
+// (cudaFree waits for the device) and zero-fills the new one on the stream,
+// which is what the GEMV split-K tickets need.  Not callable during stream
+// capture: make one call of the largest shape before capturing.
+void* workspace(DeviceState* ds, cudaStream_t s, size_t bytes) {
+    if (bytes == 0) return nullptr;
+    std::lock_guard<std::mutex> lk(ds->mu);
+    Workspace& w = ds->ws[s];
+    if (w.bytes >= bytes) return w.ptr;
+    if (w.ptr) cudaFree(w.ptr);
+    w.ptr = nullptr;
+    w.bytes = 0;
+    size_t want = bytes + bytes / 4;
+    if (cudaMalloc(&w.ptr, want) != cudaSuccess) {
+        cudaGetLastError();
+        w.ptr = nullptr;
+        return nullptr;
+    }
+    if (cudaMemsetAsync(w.ptr, 0, want, s) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(w.ptr);
+        w.ptr = nullptr;
+        return nullptr;
+    }
+    w.bytes = want;
+    return w.ptr;
+}
+
+struct ThreadState {
+    void* stream = nullptr;
+    int path = VKBLAS_PATH_AUTO;
+    int splitk = 0;
+    int last = VKBLAS_PATH_AUTO;
+};
+thread_local ThreadState tls;
+
+const char* dtype_name(int d) { return d == DT_F32 ? "f32" : d == DT_F16 ? "f16" : "bf16"; }
+const char* path_name(int p) {
+    return p == VKBLAS_PATH_SIMT ? "simt" : p == VKBLAS_PATH_TC ? "tc" : p == VKBLAS_PATH_GEMV ? "gemv" : "auto";
+}
+
+vkblas_status_t check_problem(const GemmProblem& p) {
+    if (p.M == 0 || p.N == 0 || p.K == 0 || p.batch == 0) return VKBLAS_ERR_PARAM;
+    if (!p.A || !p.B || !p.C) return VKBLAS_ERR_PARAM;
+    // Leading dimensions must cover a row of the stored matrix (the bound
+    // hipBLAS itself enforces: lda >= rows of the column-major operand).
+    if (p.lda < (p.op_a ? p.M : p.K)) return VKBLAS_ERR_PARAM;
+    if (p.ldb < (p.op_b ? p.K : p.N)) return VKBLAS_ERR_PARAM;
+    if (p.ldc < p.N) return VKBLAS_ERR_PARAM;
+    if (p.sa < 0 || p.sb < 0 || p.sc < 0) return VKBLAS_ERR_PARAM;
+    return VKBLAS_OK;
+}
+
+vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
+    vkblas_status_t st = check_problem(p);
+    if (st != VKBLAS_OK) return st;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return VKBLAS_ERR_INIT;
+    }
+    DeviceState* ds = device_state(dev);
+    if (!ds || ds->cc_major != 10) return VKBLAS_ERR_INIT;
+    const Config& cfg = config();
+    const int forced = tls.path;
+
+    int path = 0;
+    if ((forced == VKBLAS_PATH_AUTO && cfg.gemv) || forced == VKBLAS_PATH_GEMV) {
+        if (gemv_supported(p)) path = VKBLAS_PATH_GEMV;
+    }
+    if (!path && (forced == VKBLAS_PATH_AUTO || forced == VKBLAS_PATH_TC)) {
+        bool allow = forced == VKBLAS_PATH_TC ||
+                     (p.dtype == DT_F32 ? cfg.sgemm != 1 : cfg.hgemm != 1);
+        if (allow && umma_supported(p)) path = VKBLAS_PATH_TC;
+    }
+    if (!path && (forced == VKBLAS_PATH_AUTO || forced == VKBLAS_PATH_SIMT)) path = VKBLAS_PATH_SIMT;
+    if (!path) return VKBLAS_ERR_FALLBACK;
+
+    cudaError_t e = cudaSuccess;
+    int splitk = 0;
+    if (path == VKBLAS_PATH_GEMV) {
+        splitk = tls.splitk > 0 ? tls.splitk : cfg.gemv_splitk > 0 ? cfg.gemv_splitk
+                                                                   : gemv_auto_splitk(p, ds->num_sms);
+        if (splitk > 16) splitk = 16;
+        void* ws = nullptr;
+        size_t need = gemv_workspace_bytes(p, splitk);
+        if (need) {
+            ws = workspace(ds, s, need);
+            if (!ws) splitk = 1;
+        }
+        e = launch_gemv(p, splitk, ws, s);
+    } else if (path == VKBLAS_PATH_TC) {
+        e = launch_umma_gemm(p, ds->num_sms, ds->d_status, s);
+    } else {
+        e = launch_simt_gemm(p, s);
+    }
+    if (cfg.trace)
+        fprintf(stderr, "[vkblas] gemm %s %c%c M=%u N=%u K=%u lda=%u ldb=%u ldc=%u batch=%u path=%s%s%d -> %s\n",
+                dtype_name(p.dtype), p.op_a ? 'T' : 'N', p.op_b ? 'T' : 'N', p.M, p.N, p.K, p.lda,
+                p.ldb, p.ldc, p.batch, path_name(path), path == VKBLAS_PATH_GEMV ? " splitk=" : " ",
+                path == VKBLAS_PATH_GEMV ? splitk : 0, cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return e == cudaErrorInvalidValue || e == cudaErrorInvalidConfiguration ? VKBLAS_ERR_PARAM
+                                                                                 : VKBLAS_ERR_INIT;
+    }
+    tls.last = path;
+    return VKBLAS_OK;
+}
+
+GemmProblem make_problem(int dtype, vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M, uint32_t N,
+                         uint32_t K, float alpha, const void* A, uint32_t lda, const void* B,
+                         uint32_t ldb, float beta, void* C, uint32_t ldc, uint32_t batch,
+                         int64_t sa, int64_t sb, int64_t sc) {
+    GemmProblem p;
+    p.dtype = dtype;
+    p.op_a = op_a == VKBLAS_OP_T;
+    p.op_b = op_b == VKBLAS_OP_T;
+    p.M = M; p.N = N; p.K = K;
+    p.alpha = alpha; p.beta = beta;
+    p.d_alpha = nullptr; p.d_beta = nullptr;
+    p.A = A; p.lda = lda; p.B = B; p.ldb = ldb; p.C = C; p.ldc = ldc;
+    p.batch = batch;
+    // A batch of one never steps: normalise its strides.
+    p.sa = batch > 1 ? sa : 0; p.sb = batch > 1 ? sb : 0; p.sc = batch > 1 ? sc : 0;
+    return p;
+}
+
+}  // namespace
+}  // namespace vkb
+
+using namespace vkb;
+
+#define VKB_EXPORT extern "C" __attribute__((visibility("default")))
+
+VKB_EXPORT void vkblas_cache_invalidate_base(const void* ptr) { (void)ptr; }
+
+VKB_EXPORT vkblas_status_t vkblas_gemm_f32(vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M,
+                                           uint32_t N, uint32_t K, float alpha, const void* A,
+                                           uint32_t lda, const void* B, uint32_t ldb, float beta,
+                                           void* C, uint32_t ldc, uint32_t batch,
+                                           int64_t stride_a, int64_t stride_b, int64_t stride_c) {
+    GemmProblem p = make_problem(DT_F32, op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc,
+                                 batch, stride_a, stride_b, stride_c);
+    return run(p, reinterpret_cast<cudaStream_t>(tls.stream));
+}
+
+VKB_EXPORT vkblas_status_t vkblas_gemm_f16(vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M,
+                                           uint32_t N, uint32_t K, float alpha, const void* A,
+                                           uint32_t lda, const void* B, uint32_t ldb, float beta,
+                                           void* C, uint32_t ldc, uint32_t batch,
+                                           int64_t stride_a, int64_t stride_b, int64_t stride_c) {
+    GemmProblem p = make_problem(DT_F16, op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc,
+                                 batch, stride_a, stride_b, stride_c);
+    return run(p, reinterpret_cast<cudaStream_t>(tls.stream));
+}
+
+VKB_EXPORT vkblas_status_t vkblas_gemm_bf16(vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M,
+                                            uint32_t N, uint32_t K, float alpha, const void* A,
+                                            uint32_t lda, const void* B, uint32_t ldb, float beta,
+                                            void* C, uint32_t ldc, uint32_t batch,
+                                            int64_t stride_a, int64_t stride_b, int64_t stride_c) {
+    GemmProblem p = make_problem(DT_BF16, op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc,
+                                 batch, stride_a, stride_b, stride_c);
+    return run(p, reinterpret_cast<cudaStream_t>(tls.stream));
+}
+
+VKB_EXPORT vkblas_status_t vkblas_gemm_bf16_hipblas(vkblas_op_t op_a, vkblas_op_t op_b,
+                                                    uint32_t M, uint32_t N, uint32_t K,
+                                                    float alpha, const void* A, uint32_t lda,
+                                                    const void* B, uint32_t ldb, float beta,
+                                                    void* C, uint32_t ldc, uint32_t batch,
+                                                    int64_t stride_a, int64_t stride_b,
+                                                    int64_t stride_c) {
+    return vkblas_gemm_bf16(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, batch,
+                            stride_a, stride_b, stride_c);
+}
+
+VKB_EXPORT int vkblas_gemm_c64(vkblas_op_t, vkblas_op_t, uint32_t, uint32_t, uint32_t, float,
+                               float, const void*, uint32_t, const void*, uint32_t, float, float,
+                               void*, uint32_t, uint32_t, int64_t, int64_t, int64_t) {
+    return VKBLAS_ERR_FALLBACK;
+}
+
+VKB_EXPORT int vkblas_gemm_f64(vkblas_op_t, vkblas_op_t, uint32_t, uint32_t, uint32_t, double,
+                               const void*, uint32_t, const void*, uint32_t, double, void*,
+                               uint32_t, uint32_t, int64_t, int64_t, int64_t) {
+    return VKBLAS_ERR_FALLBACK;
+}
+
+VKB_EXPORT int vkblas_gemm_z64(vkblas_op_t, vkblas_op_t, uint32_t, uint32_t, uint32_t, double,
+                               double, const void*, uint32_t, const void*, uint32_t, double,
+                               double, void*, uint32_t, uint32_t, int64_t, int64_t, int64_t) {
+    return VKBLAS_ERR_FALLBACK;
+}
+
+VKB_EXPORT vkblas_status_t vkblas_gemm_ex(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op_t op_b,
+                                          uint32_t M, uint32_t N, uint32_t K, const float* alpha,
+                                          const float* beta, int scalars_on_device, const void* A,
+                                          uint32_t lda, const void* B, uint32_t ldb, void* C,
+                                          uint32_t ldc, uint32_t batch, int64_t stride_a,
+                                          int64_t stride_b, int64_t stride_c, void* stream) {
+    if (!alpha || !beta) return VKBLAS_ERR_PARAM;
+    if (dtype != VKBLAS_DT_F32 && dtype != VKBLAS_DT_F16 && dtype != VKBLAS_DT_BF16)
+        return VKBLAS_ERR_PARAM;
+    GemmProblem p = make_problem((int)dtype, op_a, op_b, M, N, K, 0.f, A, lda, B, ldb, 0.f, C, ldc,
+                                 batch, stride_a, stride_b, stride_c);
+    if (scalars_on_device) {
+        p.d_alpha = alpha;
+        p.d_beta = beta;
+    } else {
+        p.alpha = *alpha;
+        p.beta = *beta;
+    }
+    return run(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+VKB_EXPORT void vkblas_set_stream(void* stream) { tls.stream = stream; }
+VKB_EXPORT void* vkblas_get_stream(void) { return tls.stream; }
+VKB_EXPORT void vkblas_b200_set_path(int path) {
+    tls.path = (path >= VKBLAS_PATH_AUTO && path <= VKBLAS_PATH_GEMV) ? path : VKBLAS_PATH_AUTO;
+}
+VKB_EXPORT int vkblas_b200_get_path(void) { return tls.path; }
+VKB_EXPORT int vkblas_b200_last_path(void) { return tls.last; }
+VKB_EXPORT void vkblas_b200_set_splitk(int splitk) {
+    tls.splitk = splitk < 0 ? 0 : splitk > 16 ? 16 : splitk;
+}
+
+VKB_EXPORT int vkblas_b200_device_status(int clear) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    DeviceState* ds = device_state(dev);
+    if (!ds) return -1;
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    int v = 0;
+    if (cudaMemcpy(&v, ds->d_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    if (clear) cudaMemset(ds->d_status, 0, sizeof(int));
+    return v;
+}
+
+VKB_EXPORT uint64_t vkblas_b200_launch_count(void) { return g_launches.load(); }
+
+VKB_EXPORT const char* vkblas_b200_version(void) { return "vkblas-b200 0.1 (sm_100a)"; }
+
+VKB_EXPORT vkblas_status_t vkblas_shard_range(uint64_t units, uint64_t block, int rank, int world,
+                                              uint64_t* begin, uint64_t* count) {
+    if (world < 1 || rank < 0 || rank >= world || !begin || !count) return VKBLAS_ERR_PARAM;
+    if (block == 0) block = 1;
+    const uint64_t nblk = (units + block - 1) / block;
+    const uint64_t base = nblk / (uint64_t)world, rem = nblk % (uint64_t)world;
+    const uint64_t r = (uint64_t)rank;
+    const uint64_t b0 = r * base + (r < rem ? r : rem);
+    const uint64_t nb = base + (r < rem ? 1 : 0);
+    uint64_t lo = b0 * block, hi = (b0 + nb) * block;
+    if (lo > units) lo = units;
+    if (hi > units) hi = units;
+    *begin = lo;
+    *count = hi - lo;
+    return VKBLAS_OK;
+}

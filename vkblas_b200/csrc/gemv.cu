@@ -1,0 +1,284 @@
+// gemv.cu -- split-K decode GEMV for 2-byte types (M <= 16 rows of activations).
+//
+// Replaces the reference's decode family (lakitu12/vkblas src/vkblas.c:2501-2808,
+// shaders matvec_splitk_tmpl.comp, matvec_splitk_m_tmpl.comp,
+// splitk_reduce_half.comp, splitk_reduce_m_half.comp): C[m, n] = alpha *
+// sum_k X[m, k] * W[n, k] + beta * C[m, n] for M <= 16, with W stored as
+// N rows of K contiguous elements (the engine's op_b == T, i.e. hipBLAS
+// transA == T on the weights -- test/bench_decode.c:52-64).  fp32 accumulate,
+// fp32 epilogue, RNE store; with split-K the K range is cut into S segments
+// whose fp32 partials are summed in segment order before the epilogue
+// (splitk_reduce_half.comp:16-35).
+//
+// The kernel is HBM-bound on the weight stream (2*N*K bytes), so its design
+// is about bytes in flight: every lane issues 128-bit loads of W rows, four
+// per 64-wide K chunk, two chunks unrolled.  The multiply runs on the tensor
+// cores through mma.sync m16n8k16 (W rows are the MMA's M, tokens its N) so
+// that the M = 16 case is not limited by the FP32 pipe; since only the sum
+// over k matters, each lane feeds the MMA the 8 consecutive k it loaded
+// (A and B see the same k permutation), which keeps every load 128 bits wide
+// without shared memory.  Split-K partials go to a workspace; the last CTA of
+// each column block (atomic ticket, no waiting) reduces them in segment
+// order, applies alpha/beta and resets its ticket for the next launch.
+#include "common.cuh"
+
+namespace vkb {
+namespace {
+
+constexpr int WARPS = 4;                 // 64 weight rows per CTA
+constexpr int ROWS_PER_CTA = WARPS * 16;
+constexpr int KCHUNK = 64;
+
+struct GemvArgs {
+    const void* X; uint32_t ldx;          // M x K activations, k contiguous
+    const void* W; uint32_t ldw;          // N x K weights, k contiguous
+    void* C; uint32_t ldc;                // M x N output
+    uint32_t M, N, K;
+    uint32_t kspan;                       // K elements per segment (multiple of KCHUNK)
+    uint32_t splitk;
+    float alpha, beta;
+    const float* d_alpha;
+    const float* d_beta;
+    float* partial;                       // [splitk][M][N] fp32 (split-K only)
+    unsigned* tickets;                    // [gridDim.x]   (split-K only)
+};
+
+template <typename T> struct Mma;
+template <> struct Mma<__half> {
+    static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+            "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+template <> struct Mma<__nv_bfloat16> {
+    static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+            "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ldg_cached(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// Two m16n8k16 steps covering 32 consecutive k (this lane's 8 of them are in
+// w_lo (row g), w_hi (row g+8), x (token)): see the file comment.
+template <typename T>
+__device__ __forceinline__ void mma_32k(float (&d)[4], const uint4& w_lo, const uint4& w_hi,
+                                        const uint4& x) {
+    uint32_t a0[4] = {w_lo.x, w_hi.x, w_lo.y, w_hi.y};
+    Mma<T>::run(d, a0, x.x, x.y);
+    uint32_t a1[4] = {w_lo.z, w_hi.z, w_lo.w, w_hi.w};
+    Mma<T>::run(d, a1, x.z, x.w);
+}
+
+template <typename T, bool TWO_NTILES>
+__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t nbase = blockIdx.x * ROWS_PER_CTA + warp * 16;
+    const uint32_t seg = blockIdx.y;
+    const uint32_t kbeg = seg * a.kspan;
+    const uint32_t kend = min(a.K, kbeg + a.kspan);
+
+    const T* W = reinterpret_cast<const T*>(a.W);
+    const T* X = reinterpret_cast<const T*>(a.X);
+    const uint32_t r0 = nbase + g, r1 = nbase + g + 8;
+    const bool r0ok = r0 < a.N, r1ok = r1 < a.N;
+    const uint32_t x0 = g, x1 = g + 8;                // tokens of n-tile 0 and 1
+    const bool x0ok = x0 < a.M, x1ok = TWO_NTILES && x1 < a.M;
+    const T* w0p = W + (size_t)(r0ok ? r0 : 0) * a.ldw;
+    const T* w1p = W + (size_t)(r1ok ? r1 : 0) * a.ldw;
+    const T* x0p = X + (size_t)(x0ok ? x0 : 0) * a.ldx;
+    const T* x1p = X + (size_t)(x1ok ? x1 : 0) * a.ldx;
+
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+
+    uint32_t kb = kbeg;
+    // Two 64-wide chunks per iteration: 8 x 128-bit weight loads in flight per lane.
+    for (; kb + 2 * KCHUNK <= kend; kb += 2 * KCHUNK) {
+        uint4 w[2][2][2];                   // [chunk][half][row]
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t k = kb + c * KCHUNK + h * 32 + 8 * t;
+                w[c][h][0] = r0ok ? ldg_stream(w0p + k) : z;
+                w[c][h][1] = r1ok ? ldg_stream(w1p + k) : z;
+            }
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t k = kb + c * KCHUNK + h * 32 + 8 * t;
+                uint4 xa = x0ok ? ldg_cached(x0p + k) : z;
+                mma_32k<T>(d0, w[c][h][0], w[c][h][1], xa);
+                if (TWO_NTILES) {
+                    uint4 xb = x1ok ? ldg_cached(x1p + k) : z;
+                    mma_32k<T>(d1, w[c][h][0], w[c][h][1], xb);
+                }
+            }
+    }
+    // Tail: 32-wide halves; K is a multiple of 8, so each lane's 8-wide block
+    // is entirely inside or entirely outside [kb, kend).
+    for (; kb < kend; kb += 32) {
+        const uint32_t k = kb + 8 * t;
+        const bool in = k < kend;
+        uint4 wl = (in && r0ok) ? ldg_stream(w0p + k) : z;
+        uint4 wh = (in && r1ok) ? ldg_stream(w1p + k) : z;
+        uint4 xa = (in && x0ok) ? ldg_cached(x0p + k) : z;
+        mma_32k<T>(d0, wl, wh, xa);
+        if (TWO_NTILES) {
+            uint4 xb = (in && x1ok) ? ldg_cached(x1p + k) : z;
+            mma_32k<T>(d1, wl, wh, xb);
+        }
+    }
+
+    float alpha = a.alpha, beta = a.beta;
+    load_scalars(a.d_alpha, a.d_beta, alpha, beta);
+    T* C = reinterpret_cast<T*>(a.C);
+
+    // Fragment ownership: d[0]=(n=r0, m=2t) d[1]=(r0, 2t+1) d[2]=(r1, 2t) d[3]=(r1, 2t+1);
+    // n-tile 1 adds 8 to m.
+    if (a.splitk == 1) {
+#pragma unroll
+        for (int nt = 0; nt < (TWO_NTILES ? 2 : 1); nt++) {
+            const float* d = nt ? d1 : d0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t n = (i < 2) ? r0 : r1;
+                const uint32_t m = nt * 8 + 2 * t + (i & 1);
+                if (n < a.N && m < a.M) {
+                    T* cp = C + (size_t)m * a.ldc + n;
+                    const float c = (beta != 0.f) ? Elem<T>::to_f(*cp) : 0.f;
+                    *cp = Elem<T>::from_f(epilogue(alpha, d[i], beta, c));
+                }
+            }
+        }
+        return;
+    }
+
+    // Split-K: publish this segment's partials, then take a ticket.
+    float* P = a.partial + (size_t)seg * a.M * a.N;
+#pragma unroll
+    for (int nt = 0; nt < (TWO_NTILES ? 2 : 1); nt++) {
+        const float* d = nt ? d1 : d0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t n = (i < 2) ? r0 : r1;
+            const uint32_t m = nt * 8 + 2 * t + (i & 1);
+            if (n < a.N && m < a.M) __stcg(P + (size_t)m * a.N + n, d[i]);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ unsigned s_last;
+    if (threadIdx.x == 0) {
+        unsigned prev = atomicAdd(&a.tickets[blockIdx.x], 1u);
+        s_last = (prev == a.splitk - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // Last CTA of this column block: sum the partials in segment order.
+    const uint32_t ncta0 = blockIdx.x * ROWS_PER_CTA;
+    const uint32_t cells = (uint32_t)ROWS_PER_CTA * a.M;
+    for (uint32_t e = threadIdx.x; e < cells; e += WARPS * 32) {
+        const uint32_t m = e / ROWS_PER_CTA, n = ncta0 + e % ROWS_PER_CTA;
+        if (n >= a.N) continue;
+        float s = 0.f;
+        for (uint32_t q = 0; q < a.splitk; q++)
+            s = __fadd_rn(s, __ldcg(a.partial + ((size_t)q * a.M + m) * a.N + n));
+        T* cp = C + (size_t)m * a.ldc + n;
+        const float c = (beta != 0.f) ? Elem<T>::to_f(*cp) : 0.f;
+        *cp = Elem<T>::from_f(epilogue(alpha, s, beta, c));
+    }
+    if (threadIdx.x == 0) a.tickets[blockIdx.x] = 0u;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+bool gemv_supported(const GemmProblem& p) {
+    return (p.dtype == DT_F16 || p.dtype == DT_BF16) && p.M >= 1 && p.M <= 16 && p.op_a == 0 &&
+           p.op_b == 1 && p.batch == 1 && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
+           aligned16(p.A) && aligned16(p.B);
+}
+
+int gemv_auto_splitk(const GemmProblem& p, int num_sms) {
+    const uint32_t ctas = (p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+    int s = 1;
+    // Aim for >= 4 CTAs (16 warps) per SM while keeping >= 512 K per segment.
+    while (s < 16 && ctas * s < 4u * (uint32_t)num_sms && p.K / (2u * s) >= 512u) s *= 2;
+    return s;
+}
+
+static uint32_t gemv_kspan(uint32_t K, int splitk) {
+    uint32_t span = (K + splitk - 1) / splitk;
+    return (span + KCHUNK - 1) / KCHUNK * KCHUNK;
+}
+
+// Workspace layout: [tickets: MAX_TICKETS x u32, zero on entry and left zero
+// by the kernel][partials: splitk x M x N fp32].  The ticket area has a fixed
+// size so that calls with different shapes never see each other's partials
+// where they expect a zero ticket.
+constexpr size_t MAX_TICKETS = 65536;
+constexpr size_t TICKET_BYTES = MAX_TICKETS * sizeof(unsigned);
+
+size_t gemv_workspace_bytes(const GemmProblem& p, int splitk) {
+    if (splitk <= 1) return 0;
+    return TICKET_BYTES + (size_t)splitk * p.M * p.N * sizeof(float);
+}
+
+cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaStream_t s) {
+    if (splitk < 1) splitk = 1;
+    uint32_t kspan = gemv_kspan(p.K, splitk);
+    uint32_t segs = (p.K + kspan - 1) / kspan;        // may be < splitk after rounding
+    if (segs < 1) segs = 1;
+    const uint32_t ctas = (p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+    if (segs > 1 && ctas > MAX_TICKETS) return cudaErrorInvalidValue;
+    GemvArgs a;
+    a.X = p.A; a.ldx = p.lda; a.W = p.B; a.ldw = p.ldb; a.C = p.C; a.ldc = p.ldc;
+    a.M = p.M; a.N = p.N; a.K = p.K; a.kspan = kspan; a.splitk = segs;
+    a.alpha = p.alpha; a.beta = p.beta; a.d_alpha = p.d_alpha; a.d_beta = p.d_beta;
+    a.partial = nullptr; a.tickets = nullptr;
+    if (segs > 1) {
+        if (!workspace) return cudaErrorInvalidValue;
+        a.tickets = reinterpret_cast<unsigned*>(workspace);
+        a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + TICKET_BYTES);
+    }
+    dim3 grid((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA, segs);
+    const bool two = p.M > 8;
+    if (p.dtype == DT_F16) {
+        if (two) gemv_kernel<__half, true><<<grid, WARPS * 32, 0, s>>>(a);
+        else gemv_kernel<__half, false><<<grid, WARPS * 32, 0, s>>>(a);
+    } else if (p.dtype == DT_BF16) {
+        if (two) gemv_kernel<__nv_bfloat16, true><<<grid, WARPS * 32, 0, s>>>(a);
+        else gemv_kernel<__nv_bfloat16, false><<<grid, WARPS * 32, 0, s>>>(a);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace vkb

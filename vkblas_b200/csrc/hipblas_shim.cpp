@@ -1,0 +1,784 @@
+// hipblas_shim.cpp -- hipBLAS / rocBLAS ABI shim over the B200 BLAS core.
+//
+// Replaces lakitu12/vkblas src/vkblas_hipblas.c.  The exported symbols,
+// argument meanings and error codes are the reference's (see
+// include/vkblas_hipblas.h for the list and the deliberate differences).
+// Intercepted GEMMs are translated from hipBLAS's column-major convention to
+// the engine's row-major one by swapping the operands
+// (src/vkblas_hipblas.c:187-189, 234-239) and enqueued on the handle's stream;
+// everything else goes to the real library through dlsym, or reports
+// NOT_SUPPORTED when there is none (src/vkblas_hipblas.c:50-65).
+//
+// VKBLAS_REAL_HIPBLAS / VKBLAS_REAL_ROCBLAS name the real libraries to forward
+// to (defaults: libhipblas.so.2 / librocblas.so.4, as in the reference).
+#include <dlfcn.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+
+#include "vkblas_b200.h"
+#include "vkblas_hipblas.h"
+
+#define SHIM_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+constexpr uint32_t kHipMagic = 0x31484256u;   // "VBH1"
+constexpr uint32_t kRocMagic = 0x31524256u;   // "VBR1"
+
+struct ShimHandle {
+    uint32_t magic;
+    hipStream_t stream;
+    int pointer_mode;      // 0 host, 1 device (same values for hipBLAS and rocBLAS)
+    int atomics;
+    void* real;            // handle of the real library, when one is loaded
+};
+
+ShimHandle* as_hip(hipblasHandle_t h) {
+    auto* s = reinterpret_cast<ShimHandle*>(h);
+    return (s && s->magic == kHipMagic) ? s : nullptr;
+}
+ShimHandle* as_roc(rocblas_handle h) {
+    auto* s = reinterpret_cast<ShimHandle*>(h);
+    return (s && s->magic == kRocMagic) ? s : nullptr;
+}
+
+void* open_real(const char* env, const char* name, const char* fallback) {
+    const char* path = getenv(env);
+    void* h = dlopen(path && *path ? path : name, RTLD_LAZY | RTLD_LOCAL);
+    if (!h && !(path && *path)) h = dlopen(fallback, RTLD_LAZY | RTLD_LOCAL);
+    if (!h && getenv("VKBLAS_TRACE"))
+        fprintf(stderr, "[vkblas] real %s not found: %s\n", name, dlerror());
+    return h;
+}
+
+void* real_hipblas() {
+    static void* h = open_real("VKBLAS_REAL_HIPBLAS", "libhipblas.so.2", "/opt/rocm/lib/libhipblas.so.2");
+    return h;
+}
+void* real_rocblas() {
+    static void* h = open_real("VKBLAS_REAL_ROCBLAS", "librocblas.so.4", "/opt/rocm/lib/librocblas.so.4");
+    return h;
+}
+
+template <typename F>
+F hip_sym(const char* name) {
+    void* h = real_hipblas();
+    return h ? reinterpret_cast<F>(dlsym(h, name)) : nullptr;
+}
+template <typename F>
+F roc_sym(const char* name) {
+    void* h = real_rocblas();
+    return h ? reinterpret_cast<F>(dlsym(h, name)) : nullptr;
+}
+
+}  // namespace
+
+// Forward a call whose first argument is a hipBLAS handle: our handle is
+// swapped for the real library's.  NOT_SUPPORTED without a real library.
+#define FWD_H(name, handle, ...)                                                   \
+    ([&]() -> hipblasStatus_t {                                                    \
+        ShimHandle* sh_ = as_hip(handle);                                          \
+        if (!sh_) return HIPBLAS_STATUS_INVALID_VALUE;                             \
+        static auto fn_ = hip_sym<decltype(&name)>(#name);                         \
+        if (!fn_ || !sh_->real) return HIPBLAS_STATUS_NOT_SUPPORTED;               \
+        return fn_(reinterpret_cast<hipblasHandle_t>(sh_->real), __VA_ARGS__);     \
+    }())
+
+#define FWD_RC(name, handle, ...)                                                  \
+    ([&]() -> rocblas_status {                                                     \
+        ShimHandle* sh_ = as_roc(handle);                                          \
+        if (!sh_) return rocblas_status_invalid_handle;                            \
+        static auto fn_ = roc_sym<decltype(&name)>(#name);                         \
+        if (!fn_ || !sh_->real) return rocblas_status_not_implemented;             \
+        return fn_(reinterpret_cast<rocblas_handle>(sh_->real), __VA_ARGS__);      \
+    }())
+
+namespace {
+
+// hipBLAS op -> engine op.  For real types a conjugate transpose is a
+// transpose.  Returns -1 for values that are not an operation.
+int eng_op(int op) {
+    if (op == HIPBLAS_OP_N) return VKBLAS_OP_N;
+    if (op == HIPBLAS_OP_T || op == HIPBLAS_OP_C) return VKBLAS_OP_T;
+    return -1;
+}
+
+enum class Run { Done, Invalid, Fallback };
+
+// Column-major (hipBLAS) -> row-major engine call (src/vkblas_hipblas.c:234-239):
+// op_a <- transB, op_b <- transA, M <- n, N <- m, A <- B, B <- A.
+Run run_gemm(const ShimHandle* h, vkblas_dtype_t dt, int transA, int transB, int m, int n, int k,
+             const void* alpha, const void* A, int lda, long long sA, const void* B, int ldb,
+             long long sB, const void* beta, void* C, int ldc, long long sC, int batch,
+             bool exact_fp32) {
+    if (m <= 0 || n <= 0 || k <= 0 || batch <= 0) return Run::Invalid;
+    if (lda <= 0 || ldb <= 0 || ldc <= 0 || !alpha || !beta) return Run::Invalid;
+    const int oa = eng_op(transB), ob = eng_op(transA);
+    if (oa < 0 || ob < 0) return Run::Invalid;
+    const int saved = vkblas_b200_get_path();
+    if (exact_fp32) vkblas_b200_set_path(VKBLAS_PATH_SIMT);
+    vkblas_status_t st = vkblas_gemm_ex(
+        dt, (vkblas_op_t)oa, (vkblas_op_t)ob, (uint32_t)n, (uint32_t)m, (uint32_t)k,
+        reinterpret_cast<const float*>(alpha), reinterpret_cast<const float*>(beta),
+        h->pointer_mode == HIPBLAS_POINTER_MODE_DEVICE, B, (uint32_t)ldb, A, (uint32_t)lda, C,
+        (uint32_t)ldc, (uint32_t)batch, batch > 1 ? sB : 0, batch > 1 ? sA : 0,
+        batch > 1 ? sC : 0, reinterpret_cast<void*>(h->stream));
+    if (exact_fp32) vkblas_b200_set_path(saved);
+    if (st == VKBLAS_OK) return Run::Done;
+    if (st == VKBLAS_ERR_PARAM) return Run::Invalid;
+    return Run::Fallback;
+}
+
+// src/vkblas_hipblas.c:276-284
+bool is_fp32_compute(int c) { return c == HIPBLAS_COMPUTE_32F || c == HIPBLAS_COMPUTE_32F_PEDANTIC; }
+bool is_bf16_type(int t) { return t == HIP_R_16BF || t == HIPBLAS_R_16B; }
+bool is_fp16_type(int t) { return t == HIP_R_16F || t == HIPBLAS_R_16F; }
+
+const char* status_text(hipblasStatus_t s) {
+    switch (s) {
+        case HIPBLAS_STATUS_SUCCESS: return "HIPBLAS_STATUS_SUCCESS";
+        case HIPBLAS_STATUS_NOT_INITIALIZED: return "HIPBLAS_STATUS_NOT_INITIALIZED";
+        case HIPBLAS_STATUS_ALLOC_FAILED: return "HIPBLAS_STATUS_ALLOC_FAILED";
+        case HIPBLAS_STATUS_INVALID_VALUE: return "HIPBLAS_STATUS_INVALID_VALUE";
+        case HIPBLAS_STATUS_MAPPING_ERROR: return "HIPBLAS_STATUS_MAPPING_ERROR";
+        case HIPBLAS_STATUS_EXECUTION_FAILED: return "HIPBLAS_STATUS_EXECUTION_FAILED";
+        case HIPBLAS_STATUS_INTERNAL_ERROR: return "HIPBLAS_STATUS_INTERNAL_ERROR";
+        case HIPBLAS_STATUS_NOT_SUPPORTED: return "HIPBLAS_STATUS_NOT_SUPPORTED";
+        case HIPBLAS_STATUS_ARCH_MISMATCH: return "HIPBLAS_STATUS_ARCH_MISMATCH";
+        case HIPBLAS_STATUS_HANDLE_IS_NULLPTR: return "HIPBLAS_STATUS_HANDLE_IS_NULLPTR";
+        case HIPBLAS_STATUS_INVALID_ENUM: return "HIPBLAS_STATUS_INVALID_ENUM";
+        default: return "HIPBLAS_STATUS_UNKNOWN";
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ handle calls
+SHIM_EXPORT hipblasStatus_t hipblasCreate(hipblasHandle_t* handle) {
+    if (!handle) return HIPBLAS_STATUS_INVALID_VALUE;
+    auto* h = new ShimHandle{kHipMagic, nullptr, HIPBLAS_POINTER_MODE_HOST, 0, nullptr};
+    static auto real_create = hip_sym<hipblasStatus_t (*)(hipblasHandle_t*)>("hipblasCreate");
+    if (real_create) {
+        hipblasHandle_t r = nullptr;
+        if (real_create(&r) == HIPBLAS_STATUS_SUCCESS) h->real = r;
+    }
+    *handle = reinterpret_cast<hipblasHandle_t>(h);
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasDestroy(hipblasHandle_t handle) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    if (h->real) {
+        static auto fn = hip_sym<hipblasStatus_t (*)(hipblasHandle_t)>("hipblasDestroy");
+        if (fn) fn(reinterpret_cast<hipblasHandle_t>(h->real));
+    }
+    h->magic = 0;
+    delete h;
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasSetStream(hipblasHandle_t handle, hipStream_t streamId) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    h->stream = streamId;
+    if (h->real) return FWD_H(hipblasSetStream, handle, streamId);
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasGetStream(hipblasHandle_t handle, hipStream_t* streamId) {
+    ShimHandle* h = as_hip(handle);
+    if (!h || !streamId) return HIPBLAS_STATUS_INVALID_VALUE;
+    *streamId = h->stream;
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasSetPointerMode(hipblasHandle_t handle, hipblasPointerMode_t mode) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    if (mode != HIPBLAS_POINTER_MODE_HOST && mode != HIPBLAS_POINTER_MODE_DEVICE)
+        return HIPBLAS_STATUS_INVALID_VALUE;
+    h->pointer_mode = mode;
+    if (h->real) return FWD_H(hipblasSetPointerMode, handle, mode);
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasGetPointerMode(hipblasHandle_t handle, hipblasPointerMode_t* mode) {
+    ShimHandle* h = as_hip(handle);
+    if (!h || !mode) return HIPBLAS_STATUS_INVALID_VALUE;
+    *mode = (hipblasPointerMode_t)h->pointer_mode;
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasSetAtomicsMode(hipblasHandle_t handle, hipblasAtomicsMode_t atomics_mode) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    h->atomics = atomics_mode;      // the kernels are deterministic either way
+    if (h->real) return FWD_H(hipblasSetAtomicsMode, handle, atomics_mode);
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+// src/vkblas_hipblas.c:105-112: workspace is the library's own business.
+SHIM_EXPORT hipblasStatus_t hipblasSetWorkspace(hipblasHandle_t handle, void* workspace, size_t size) {
+    if (!as_hip(handle)) return HIPBLAS_STATUS_INVALID_VALUE;
+    (void)workspace;
+    (void)size;
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasGetVersion(hipblasHandle_t handle, int* version) {
+    ShimHandle* h = as_hip(handle);
+    if (!h || !version) return HIPBLAS_STATUS_INVALID_VALUE;
+    if (h->real) return FWD_H(hipblasGetVersion, handle, version);
+    *version = 100;   // this library: 0.1.0 in hipBLAS's major*100000 + minor*100 + patch form
+    return HIPBLAS_STATUS_SUCCESS;
+}
+
+SHIM_EXPORT const char* hipblasStatusToString(hipblasStatus_t status) {
+    static auto fn = hip_sym<const char* (*)(hipblasStatus_t)>("hipblasStatusToString");
+    return fn ? fn(status) : status_text(status);
+}
+
+// ------------------------------------------------------- intercepted GEMMs
+SHIM_EXPORT hipblasStatus_t hipblasSgemm(hipblasHandle_t handle, hipblasOperation_t transA,
+                                         hipblasOperation_t transB, int m, int n, int k,
+                                         const float* alpha, const float* AP, int lda,
+                                         const float* BP, int ldb, const float* beta, float* CP,
+                                         int ldc) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    Run r = run_gemm(h, VKBLAS_DT_F32, transA, transB, m, n, k, alpha, AP, lda, 0, BP, ldb, 0,
+                     beta, CP, ldc, 0, 1, false);
+    if (r == Run::Done) return HIPBLAS_STATUS_SUCCESS;
+    if (r == Run::Invalid) return HIPBLAS_STATUS_INVALID_VALUE;
+    return FWD_H(hipblasSgemm, handle, transA, transB, m, n, k, alpha, AP, lda, BP, ldb, beta, CP, ldc);
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasSgemmStridedBatched(hipblasHandle_t handle,
+                                                       hipblasOperation_t transA,
+                                                       hipblasOperation_t transB, int m, int n,
+                                                       int k, const float* alpha, const float* AP,
+                                                       int lda, long long strideA,
+                                                       const float* BP, int ldb, long long strideB,
+                                                       const float* beta, float* CP, int ldc,
+                                                       long long strideC, int batchCount) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    Run r = run_gemm(h, VKBLAS_DT_F32, transA, transB, m, n, k, alpha, AP, lda, strideA, BP, ldb,
+                     strideB, beta, CP, ldc, strideC, batchCount, false);
+    if (r == Run::Done) return HIPBLAS_STATUS_SUCCESS;
+    if (r == Run::Invalid) return HIPBLAS_STATUS_INVALID_VALUE;
+    return FWD_H(hipblasSgemmStridedBatched, handle, transA, transB, m, n, k, alpha, AP, lda,
+                 strideA, BP, ldb, strideB, beta, CP, ldc, strideC, batchCount);
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasGemmEx_v2(hipblasHandle_t handle, hipblasOperation_t transA,
+                                             hipblasOperation_t transB, int m, int n, int k,
+                                             const void* alpha, const void* A, hipDataType aType,
+                                             int lda, const void* B, hipDataType bType, int ldb,
+                                             const void* beta, void* C, hipDataType cType, int ldc,
+                                             hipblasComputeType_t computeType,
+                                             hipblasGemmAlgo_t algo) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    int dt = -1;
+    if (aType == HIP_R_32F && bType == HIP_R_32F && cType == HIP_R_32F && is_fp32_compute(computeType))
+        dt = VKBLAS_DT_F32;
+    else if (is_bf16_type(aType) && is_bf16_type(bType) && is_bf16_type(cType))
+        dt = VKBLAS_DT_BF16;
+    else if (is_fp16_type(aType) && is_fp16_type(bType) && is_fp16_type(cType))
+        dt = VKBLAS_DT_F16;
+    if (dt >= 0) {
+        Run r = run_gemm(h, (vkblas_dtype_t)dt, transA, transB, m, n, k, alpha, A, lda, 0, B, ldb, 0,
+                         beta, C, ldc, 0, 1, computeType == HIPBLAS_COMPUTE_32F_PEDANTIC);
+        if (r == Run::Done) return HIPBLAS_STATUS_SUCCESS;
+        if (r == Run::Invalid) return HIPBLAS_STATUS_INVALID_VALUE;
+    }
+    return FWD_H(hipblasGemmEx_v2, handle, transA, transB, m, n, k, alpha, A, aType, lda, B, bType,
+                 ldb, beta, C, cType, ldc, computeType, algo);
+}
+
+SHIM_EXPORT hipblasStatus_t hipblasGemmStridedBatchedEx_v2(
+    hipblasHandle_t handle, hipblasOperation_t transA, hipblasOperation_t transB, int m, int n,
+    int k, const void* alpha, const void* A, hipDataType aType, int lda, hipblasStride strideA,
+    const void* B, hipDataType bType, int ldb, hipblasStride strideB, const void* beta, void* C,
+    hipDataType cType, int ldc, hipblasStride strideC, int batchCount,
+    hipblasComputeType_t computeType, hipblasGemmAlgo_t algo) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    int dt = -1;
+    if (aType == HIP_R_32F && bType == HIP_R_32F && cType == HIP_R_32F && is_fp32_compute(computeType))
+        dt = VKBLAS_DT_F32;
+    else if (is_bf16_type(aType) && is_bf16_type(bType) && is_bf16_type(cType))
+        dt = VKBLAS_DT_BF16;
+    else if (is_fp16_type(aType) && is_fp16_type(bType) && is_fp16_type(cType))
+        dt = VKBLAS_DT_F16;
+    if (dt >= 0) {
+        Run r = run_gemm(h, (vkblas_dtype_t)dt, transA, transB, m, n, k, alpha, A, lda, strideA, B,
+                         ldb, strideB, beta, C, ldc, strideC, batchCount,
+                         computeType == HIPBLAS_COMPUTE_32F_PEDANTIC);
+        if (r == Run::Done) return HIPBLAS_STATUS_SUCCESS;
+        if (r == Run::Invalid) return HIPBLAS_STATUS_INVALID_VALUE;
+    }
+    return FWD_H(hipblasGemmStridedBatchedEx_v2, handle, transA, transB, m, n, k, alpha, A, aType,
+                 lda, strideA, B, bType, ldb, strideB, beta, C, cType, ldc, strideC, batchCount,
+                 computeType, algo);
+}
+
+// Legacy-typed GemmEx: fp16 and bf16 only, fp32 is forwarded
+// (src/vkblas_hipblas.c:454-466).
+SHIM_EXPORT hipblasStatus_t hipblasGemmEx(hipblasHandle_t handle, hipblasOperation_t transA,
+                                          hipblasOperation_t transB, int m, int n, int k,
+                                          const void* alpha, const void* A, hipblasDatatype_t aType,
+                                          int lda, const void* B, hipblasDatatype_t bType, int ldb,
+                                          const void* beta, void* C, hipblasDatatype_t cType,
+                                          int ldc, vkblas_gemmex_compute_t computeType,
+                                          hipblasGemmAlgo_t algo) {
+    ShimHandle* h = as_hip(handle);
+    if (!h) return HIPBLAS_STATUS_INVALID_VALUE;
+    int dt = -1;
+    if (is_bf16_type(aType) && is_bf16_type(bType) && is_bf16_type(cType)) dt = VKBLAS_DT_BF16;
+    else if (is_fp16_type(aType) && is_fp16_type(bType) && is_fp16_type(cType)) dt = VKBLAS_DT_F16;
+    if (dt >= 0) {
+        Run r = run_gemm(h, (vkblas_dtype_t)dt, transA, transB, m, n, k, alpha, A, lda, 0, B, ldb, 0,
+                         beta, C, ldc, 0, 1, false);
+        if (r == Run::Done) return HIPBLAS_STATUS_SUCCESS;
+        if (r == Run::Invalid) return HIPBLAS_STATUS_INVALID_VALUE;
+    }
+    return FWD_H(hipblasGemmEx, handle, transA, transB, m, n, k, alpha, A, aType, lda, B, bType,
+                 ldb, beta, C, cType, ldc, computeType, algo);
+}
+
+// --------------------------------------------- fp64 / complex GEMMs: forward
+#define CHECK_MNK(m, n, k)                                                        \
+    do {                                                                          \
+        if (!as_hip(handle)) return HIPBLAS_STATUS_INVALID_VALUE;                 \
+        if ((m) <= 0 || (n) <= 0 || (k) <= 0) return HIPBLAS_STATUS_INVALID_VALUE; \
+    } while (0)
+
+SHIM_EXPORT hipblasStatus_t hipblasDgemm(hipblasHandle_t handle, hipblasOperation_t transA,
+                                         hipblasOperation_t transB, int m, int n, int k,
+                                         const double* alpha, const double* AP, int lda,
+                                         const double* BP, int ldb, const double* beta,
+                                         double* CP, int ldc) {
+    CHECK_MNK(m, n, k);
+    return FWD_H(hipblasDgemm, handle, transA, transB, m, n, k, alpha, AP, lda, BP, ldb, beta, CP, ldc);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDgemmStridedBatched(
+    hipblasHandle_t handle, hipblasOperation_t transA, hipblasOperation_t transB, int m, int n,
+    int k, const double* alpha, const double* AP, int lda, long long strideA, const double* BP,
+    int ldb, long long strideB, const double* beta, double* CP, int ldc, long long strideC,
+    int batchCount) {
+    CHECK_MNK(m, n, k);
+    if (batchCount <= 0) return HIPBLAS_STATUS_INVALID_VALUE;
+    return FWD_H(hipblasDgemmStridedBatched, handle, transA, transB, m, n, k, alpha, AP, lda,
+                 strideA, BP, ldb, strideB, beta, CP, ldc, strideC, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCgemm_v2(hipblasHandle_t handle, hipblasOperation_t transA,
+                                            hipblasOperation_t transB, int m, int n, int k,
+                                            const hipComplex* alpha, const hipComplex* AP, int lda,
+                                            const hipComplex* BP, int ldb, const hipComplex* beta,
+                                            hipComplex* CP, int ldc) {
+    CHECK_MNK(m, n, k);
+    return FWD_H(hipblasCgemm_v2, handle, transA, transB, m, n, k, alpha, AP, lda, BP, ldb, beta, CP, ldc);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCgemmStridedBatched_v2(
+    hipblasHandle_t handle, hipblasOperation_t transA, hipblasOperation_t transB, int m, int n,
+    int k, const hipComplex* alpha, const hipComplex* AP, int lda, long long strideA,
+    const hipComplex* BP, int ldb, long long strideB, const hipComplex* beta, hipComplex* CP,
+    int ldc, long long strideC, int batchCount) {
+    CHECK_MNK(m, n, k);
+    if (batchCount <= 0) return HIPBLAS_STATUS_INVALID_VALUE;
+    return FWD_H(hipblasCgemmStridedBatched_v2, handle, transA, transB, m, n, k, alpha, AP, lda,
+                 strideA, BP, ldb, strideB, beta, CP, ldc, strideC, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZgemm_v2(hipblasHandle_t handle, hipblasOperation_t transA,
+                                            hipblasOperation_t transB, int m, int n, int k,
+                                            const hipDoubleComplex* alpha,
+                                            const hipDoubleComplex* AP, int lda,
+                                            const hipDoubleComplex* BP, int ldb,
+                                            const hipDoubleComplex* beta, hipDoubleComplex* CP,
+                                            int ldc) {
+    CHECK_MNK(m, n, k);
+    return FWD_H(hipblasZgemm_v2, handle, transA, transB, m, n, k, alpha, AP, lda, BP, ldb, beta, CP, ldc);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZgemmStridedBatched_v2(
+    hipblasHandle_t handle, hipblasOperation_t transA, hipblasOperation_t transB, int m, int n,
+    int k, const hipDoubleComplex* alpha, const hipDoubleComplex* AP, int lda, long long strideA,
+    const hipDoubleComplex* BP, int ldb, long long strideB, const hipDoubleComplex* beta,
+    hipDoubleComplex* CP, int ldc, long long strideC, int batchCount) {
+    CHECK_MNK(m, n, k);
+    if (batchCount <= 0) return HIPBLAS_STATUS_INVALID_VALUE;
+    return FWD_H(hipblasZgemmStridedBatched_v2, handle, transA, transB, m, n, k, alpha, AP, lda,
+                 strideA, BP, ldb, strideB, beta, CP, ldc, strideC, batchCount);
+}
+
+// ------------------------------- dot / gemv / trsm / factorisations: forward
+// (src/vkblas_hipblas.c:632-800)
+SHIM_EXPORT hipblasStatus_t hipblasSdot(hipblasHandle_t handle, int n, const float* x, int incx,
+                                        const float* y, int incy, float* result) {
+    return FWD_H(hipblasSdot, handle, n, x, incx, y, incy, result);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDdot(hipblasHandle_t handle, int n, const double* x, int incx,
+                                        const double* y, int incy, double* result) {
+    return FWD_H(hipblasDdot, handle, n, x, incx, y, incy, result);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCdotc_v2(hipblasHandle_t handle, int n, const hipComplex* x,
+                                            int incx, const hipComplex* y, int incy,
+                                            hipComplex* result) {
+    return FWD_H(hipblasCdotc_v2, handle, n, x, incx, y, incy, result);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCdotu_v2(hipblasHandle_t handle, int n, const hipComplex* x,
+                                            int incx, const hipComplex* y, int incy,
+                                            hipComplex* result) {
+    return FWD_H(hipblasCdotu_v2, handle, n, x, incx, y, incy, result);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZdotc_v2(hipblasHandle_t handle, int n,
+                                            const hipDoubleComplex* x, int incx,
+                                            const hipDoubleComplex* y, int incy,
+                                            hipDoubleComplex* result) {
+    return FWD_H(hipblasZdotc_v2, handle, n, x, incx, y, incy, result);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZdotu_v2(hipblasHandle_t handle, int n,
+                                            const hipDoubleComplex* x, int incx,
+                                            const hipDoubleComplex* y, int incy,
+                                            hipDoubleComplex* result) {
+    return FWD_H(hipblasZdotu_v2, handle, n, x, incx, y, incy, result);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDotEx_v2(hipblasHandle_t handle, int n, const void* x,
+                                            hipDataType xType, int incx, const void* y,
+                                            hipDataType yType, int incy, void* result,
+                                            hipDataType resultType, hipDataType executionType) {
+    return FWD_H(hipblasDotEx_v2, handle, n, x, xType, incx, y, yType, incy, result, resultType,
+                 executionType);
+}
+SHIM_EXPORT hipblasStatus_t hipblasSgemv(hipblasHandle_t handle, hipblasOperation_t trans, int m,
+                                         int n, const float* alpha, const float* AP, int lda,
+                                         const float* x, int incx, const float* beta, float* y,
+                                         int incy) {
+    return FWD_H(hipblasSgemv, handle, trans, m, n, alpha, AP, lda, x, incx, beta, y, incy);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDgemv(hipblasHandle_t handle, hipblasOperation_t trans, int m,
+                                         int n, const double* alpha, const double* AP, int lda,
+                                         const double* x, int incx, const double* beta, double* y,
+                                         int incy) {
+    return FWD_H(hipblasDgemv, handle, trans, m, n, alpha, AP, lda, x, incx, beta, y, incy);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCgemv_v2(hipblasHandle_t handle, hipblasOperation_t trans,
+                                            int m, int n, const hipComplex* alpha,
+                                            const hipComplex* AP, int lda, const hipComplex* x,
+                                            int incx, const hipComplex* beta, hipComplex* y,
+                                            int incy) {
+    return FWD_H(hipblasCgemv_v2, handle, trans, m, n, alpha, AP, lda, x, incx, beta, y, incy);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZgemv_v2(hipblasHandle_t handle, hipblasOperation_t trans,
+                                            int m, int n, const hipDoubleComplex* alpha,
+                                            const hipDoubleComplex* AP, int lda,
+                                            const hipDoubleComplex* x, int incx,
+                                            const hipDoubleComplex* beta, hipDoubleComplex* y,
+                                            int incy) {
+    return FWD_H(hipblasZgemv_v2, handle, trans, m, n, alpha, AP, lda, x, incx, beta, y, incy);
+}
+SHIM_EXPORT hipblasStatus_t hipblasStrsm(hipblasHandle_t handle, hipblasSideMode_t side,
+                                         hipblasFillMode_t uplo, hipblasOperation_t transA,
+                                         hipblasDiagType_t diag, int m, int n, const float* alpha,
+                                         const float* AP, int lda, float* BP, int ldb) {
+    return FWD_H(hipblasStrsm, handle, side, uplo, transA, diag, m, n, alpha, AP, lda, BP, ldb);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDtrsm(hipblasHandle_t handle, hipblasSideMode_t side,
+                                         hipblasFillMode_t uplo, hipblasOperation_t transA,
+                                         hipblasDiagType_t diag, int m, int n, const double* alpha,
+                                         const double* AP, int lda, double* BP, int ldb) {
+    return FWD_H(hipblasDtrsm, handle, side, uplo, transA, diag, m, n, alpha, AP, lda, BP, ldb);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCtrsm_v2(hipblasHandle_t handle, hipblasSideMode_t side,
+                                            hipblasFillMode_t uplo, hipblasOperation_t transA,
+                                            hipblasDiagType_t diag, int m, int n,
+                                            const hipComplex* alpha, const hipComplex* AP, int lda,
+                                            hipComplex* BP, int ldb) {
+    return FWD_H(hipblasCtrsm_v2, handle, side, uplo, transA, diag, m, n, alpha, AP, lda, BP, ldb);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZtrsm_v2(hipblasHandle_t handle, hipblasSideMode_t side,
+                                            hipblasFillMode_t uplo, hipblasOperation_t transA,
+                                            hipblasDiagType_t diag, int m, int n,
+                                            const hipDoubleComplex* alpha,
+                                            const hipDoubleComplex* AP, int lda,
+                                            hipDoubleComplex* BP, int ldb) {
+    return FWD_H(hipblasZtrsm_v2, handle, side, uplo, transA, diag, m, n, alpha, AP, lda, BP, ldb);
+}
+SHIM_EXPORT hipblasStatus_t hipblasStrsmBatched(hipblasHandle_t handle, hipblasSideMode_t side,
+                                                hipblasFillMode_t uplo, hipblasOperation_t transA,
+                                                hipblasDiagType_t diag, int m, int n,
+                                                const float* alpha, const float* const AP[],
+                                                int lda, float* const BP[], int ldb,
+                                                int batchCount) {
+    return FWD_H(hipblasStrsmBatched, handle, side, uplo, transA, diag, m, n, alpha, AP, lda, BP,
+                 ldb, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDtrsmBatched(hipblasHandle_t handle, hipblasSideMode_t side,
+                                                hipblasFillMode_t uplo, hipblasOperation_t transA,
+                                                hipblasDiagType_t diag, int m, int n,
+                                                const double* alpha, const double* const AP[],
+                                                int lda, double* const BP[], int ldb,
+                                                int batchCount) {
+    return FWD_H(hipblasDtrsmBatched, handle, side, uplo, transA, diag, m, n, alpha, AP, lda, BP,
+                 ldb, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCtrsmBatched_v2(hipblasHandle_t handle, hipblasSideMode_t side,
+                                                   hipblasFillMode_t uplo,
+                                                   hipblasOperation_t transA,
+                                                   hipblasDiagType_t diag, int m, int n,
+                                                   const hipComplex* alpha,
+                                                   const hipComplex* const AP[], int lda,
+                                                   hipComplex* const BP[], int ldb,
+                                                   int batchCount) {
+    return FWD_H(hipblasCtrsmBatched_v2, handle, side, uplo, transA, diag, m, n, alpha, AP, lda,
+                 BP, ldb, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZtrsmBatched_v2(hipblasHandle_t handle, hipblasSideMode_t side,
+                                                   hipblasFillMode_t uplo,
+                                                   hipblasOperation_t transA,
+                                                   hipblasDiagType_t diag, int m, int n,
+                                                   const hipDoubleComplex* alpha,
+                                                   const hipDoubleComplex* const AP[], int lda,
+                                                   hipDoubleComplex* const BP[], int ldb,
+                                                   int batchCount) {
+    return FWD_H(hipblasZtrsmBatched_v2, handle, side, uplo, transA, diag, m, n, alpha, AP, lda,
+                 BP, ldb, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasSgelsBatched(hipblasHandle_t handle, hipblasOperation_t trans,
+                                                const int m, const int n, const int nrhs,
+                                                float* const A[], const int lda, float* const B[],
+                                                const int ldb, int* info, int* deviceInfo,
+                                                const int batchCount) {
+    return FWD_H(hipblasSgelsBatched, handle, trans, m, n, nrhs, A, lda, B, ldb, info, deviceInfo,
+                 batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDgelsBatched(hipblasHandle_t handle, hipblasOperation_t trans,
+                                                const int m, const int n, const int nrhs,
+                                                double* const A[], const int lda,
+                                                double* const B[], const int ldb, int* info,
+                                                int* deviceInfo, const int batchCount) {
+    return FWD_H(hipblasDgelsBatched, handle, trans, m, n, nrhs, A, lda, B, ldb, info, deviceInfo,
+                 batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCgelsBatched_v2(hipblasHandle_t handle,
+                                                   hipblasOperation_t trans, const int m,
+                                                   const int n, const int nrhs,
+                                                   hipComplex* const A[], const int lda,
+                                                   hipComplex* const B[], const int ldb, int* info,
+                                                   int* deviceInfo, const int batchCount) {
+    return FWD_H(hipblasCgelsBatched_v2, handle, trans, m, n, nrhs, A, lda, B, ldb, info,
+                 deviceInfo, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZgelsBatched_v2(hipblasHandle_t handle,
+                                                   hipblasOperation_t trans, const int m,
+                                                   const int n, const int nrhs,
+                                                   hipDoubleComplex* const A[], const int lda,
+                                                   hipDoubleComplex* const B[], const int ldb,
+                                                   int* info, int* deviceInfo,
+                                                   const int batchCount) {
+    return FWD_H(hipblasZgelsBatched_v2, handle, trans, m, n, nrhs, A, lda, B, ldb, info,
+                 deviceInfo, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasSgeqrfBatched(hipblasHandle_t handle, const int m, const int n,
+                                                 float* const A[], const int lda,
+                                                 float* const ipiv[], int* info,
+                                                 const int batchCount) {
+    return FWD_H(hipblasSgeqrfBatched, handle, m, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDgeqrfBatched(hipblasHandle_t handle, const int m, const int n,
+                                                 double* const A[], const int lda,
+                                                 double* const ipiv[], int* info,
+                                                 const int batchCount) {
+    return FWD_H(hipblasDgeqrfBatched, handle, m, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCgeqrfBatched_v2(hipblasHandle_t handle, const int m,
+                                                    const int n, hipComplex* const A[],
+                                                    const int lda, hipComplex* const ipiv[],
+                                                    int* info, const int batchCount) {
+    return FWD_H(hipblasCgeqrfBatched_v2, handle, m, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZgeqrfBatched_v2(hipblasHandle_t handle, const int m,
+                                                    const int n, hipDoubleComplex* const A[],
+                                                    const int lda, hipDoubleComplex* const ipiv[],
+                                                    int* info, const int batchCount) {
+    return FWD_H(hipblasZgeqrfBatched_v2, handle, m, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasSgetrfBatched(hipblasHandle_t handle, const int n,
+                                                 float* const A[], const int lda, int* ipiv,
+                                                 int* info, const int batchCount) {
+    return FWD_H(hipblasSgetrfBatched, handle, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDgetrfBatched(hipblasHandle_t handle, const int n,
+                                                 double* const A[], const int lda, int* ipiv,
+                                                 int* info, const int batchCount) {
+    return FWD_H(hipblasDgetrfBatched, handle, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCgetrfBatched_v2(hipblasHandle_t handle, const int n,
+                                                    hipComplex* const A[], const int lda,
+                                                    int* ipiv, int* info, const int batchCount) {
+    return FWD_H(hipblasCgetrfBatched_v2, handle, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZgetrfBatched_v2(hipblasHandle_t handle, const int n,
+                                                    hipDoubleComplex* const A[], const int lda,
+                                                    int* ipiv, int* info, const int batchCount) {
+    return FWD_H(hipblasZgetrfBatched_v2, handle, n, A, lda, ipiv, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasSgetrsBatched(hipblasHandle_t handle,
+                                                 const hipblasOperation_t trans, const int n,
+                                                 const int nrhs, float* const A[], const int lda,
+                                                 const int* ipiv, float* const B[], const int ldb,
+                                                 int* info, const int batchCount) {
+    return FWD_H(hipblasSgetrsBatched, handle, trans, n, nrhs, A, lda, ipiv, B, ldb, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasDgetrsBatched(hipblasHandle_t handle,
+                                                 const hipblasOperation_t trans, const int n,
+                                                 const int nrhs, double* const A[], const int lda,
+                                                 const int* ipiv, double* const B[], const int ldb,
+                                                 int* info, const int batchCount) {
+    return FWD_H(hipblasDgetrsBatched, handle, trans, n, nrhs, A, lda, ipiv, B, ldb, info, batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasCgetrsBatched_v2(hipblasHandle_t handle,
+                                                    const hipblasOperation_t trans, const int n,
+                                                    const int nrhs, hipComplex* const A[],
+                                                    const int lda, const int* ipiv,
+                                                    hipComplex* const B[], const int ldb,
+                                                    int* info, const int batchCount) {
+    return FWD_H(hipblasCgetrsBatched_v2, handle, trans, n, nrhs, A, lda, ipiv, B, ldb, info,
+                 batchCount);
+}
+SHIM_EXPORT hipblasStatus_t hipblasZgetrsBatched_v2(hipblasHandle_t handle,
+                                                    const hipblasOperation_t trans, const int n,
+                                                    const int nrhs, hipDoubleComplex* const A[],
+                                                    const int lda, const int* ipiv,
+                                                    hipDoubleComplex* const B[], const int ldb,
+                                                    int* info, const int batchCount) {
+    return FWD_H(hipblasZgetrsBatched_v2, handle, trans, n, nrhs, A, lda, ipiv, B, ldb, info,
+                 batchCount);
+}
+
+// ================================================================ rocBLAS
+SHIM_EXPORT rocblas_status rocblas_create_handle(rocblas_handle* handle) {
+    if (!handle) return rocblas_status_invalid_pointer;
+    auto* h = new ShimHandle{kRocMagic, nullptr, rocblas_pointer_mode_host, 0, nullptr};
+    static auto real_create = roc_sym<rocblas_status (*)(rocblas_handle*)>("rocblas_create_handle");
+    if (real_create) {
+        rocblas_handle r = nullptr;
+        if (real_create(&r) == rocblas_status_success) h->real = r;
+    }
+    *handle = reinterpret_cast<rocblas_handle>(h);
+    return rocblas_status_success;
+}
+
+SHIM_EXPORT rocblas_status rocblas_destroy_handle(rocblas_handle handle) {
+    ShimHandle* h = as_roc(handle);
+    if (!h) return rocblas_status_invalid_handle;
+    if (h->real) {
+        static auto fn = roc_sym<rocblas_status (*)(rocblas_handle)>("rocblas_destroy_handle");
+        if (fn) fn(reinterpret_cast<rocblas_handle>(h->real));
+    }
+    h->magic = 0;
+    delete h;
+    return rocblas_status_success;
+}
+
+SHIM_EXPORT rocblas_status rocblas_set_stream(rocblas_handle handle, hipStream_t stream) {
+    ShimHandle* h = as_roc(handle);
+    if (!h) return rocblas_status_invalid_handle;
+    h->stream = stream;
+    if (h->real) return FWD_RC(rocblas_set_stream, handle, stream);
+    return rocblas_status_success;
+}
+
+SHIM_EXPORT rocblas_status rocblas_get_stream(rocblas_handle handle, hipStream_t* stream) {
+    ShimHandle* h = as_roc(handle);
+    if (!h) return rocblas_status_invalid_handle;
+    if (!stream) return rocblas_status_invalid_pointer;
+    *stream = h->stream;
+    return rocblas_status_success;
+}
+
+SHIM_EXPORT rocblas_status rocblas_set_pointer_mode(rocblas_handle handle, rocblas_pointer_mode mode) {
+    ShimHandle* h = as_roc(handle);
+    if (!h) return rocblas_status_invalid_handle;
+    if (mode != rocblas_pointer_mode_host && mode != rocblas_pointer_mode_device)
+        return rocblas_status_invalid_value;
+    h->pointer_mode = mode;
+    if (h->real) return FWD_RC(rocblas_set_pointer_mode, handle, mode);
+    return rocblas_status_success;
+}
+
+SHIM_EXPORT rocblas_status rocblas_get_pointer_mode(rocblas_handle handle, rocblas_pointer_mode* mode) {
+    ShimHandle* h = as_roc(handle);
+    if (!h) return rocblas_status_invalid_handle;
+    if (!mode) return rocblas_status_invalid_pointer;
+    *mode = (rocblas_pointer_mode)h->pointer_mode;
+    return rocblas_status_success;
+}
+
+namespace {
+int roc_dtype(rocblas_datatype a, rocblas_datatype b, rocblas_datatype c, rocblas_datatype d) {
+    if (a == rocblas_datatype_f16_r && b == a && c == a && d == a) return VKBLAS_DT_F16;
+    if (a == rocblas_datatype_bf16_r && b == a && c == a && d == a) return VKBLAS_DT_BF16;
+    if (a == rocblas_datatype_f32_r && b == a && c == a && d == a) return VKBLAS_DT_F32;
+    return -1;
+}
+int roc_to_hip_op(rocblas_operation o) {
+    return o == rocblas_operation_none ? HIPBLAS_OP_N
+         : o == rocblas_operation_transpose ? HIPBLAS_OP_T
+         : o == rocblas_operation_conjugate_transpose ? HIPBLAS_OP_C : -1;
+}
+}  // namespace
+
+// src/vkblas_hipblas.c:828-891
+SHIM_EXPORT rocblas_status rocblas_gemm_ex(rocblas_handle handle, rocblas_operation transA,
+                                           rocblas_operation transB, rocblas_int m, rocblas_int n,
+                                           rocblas_int k, const void* alpha, const void* a,
+                                           rocblas_datatype a_type, rocblas_int lda, const void* b,
+                                           rocblas_datatype b_type, rocblas_int ldb,
+                                           const void* beta, const void* c,
+                                           rocblas_datatype c_type, rocblas_int ldc, void* d,
+                                           rocblas_datatype d_type, rocblas_int ldd,
+                                           rocblas_datatype compute_type, rocblas_gemm_algo algo,
+                                           int32_t solution_index, uint32_t flags) {
+    ShimHandle* h = as_roc(handle);
+    if (!h) return rocblas_status_invalid_value;
+    if (m <= 0 || n <= 0 || k <= 0) return rocblas_status_invalid_value;
+    int dt = roc_dtype(a_type, b_type, c_type, d_type);
+    if (c == d && ldc == ldd && compute_type == rocblas_datatype_f32_r && dt >= 0) {
+        Run r = run_gemm(h, (vkblas_dtype_t)dt, roc_to_hip_op(transA), roc_to_hip_op(transB), m, n,
+                         k, alpha, a, lda, 0, b, ldb, 0, beta, d, ldd, 0, 1, false);
+        if (r == Run::Done) return rocblas_status_success;
+        if (r == Run::Invalid) return rocblas_status_invalid_value;
+    }
+    return FWD_RC(rocblas_gemm_ex, handle, transA, transB, m, n, k, alpha, a, a_type, lda, b,
+                  b_type, ldb, beta, c, c_type, ldc, d, d_type, ldd, compute_type, algo,
+                  solution_index, flags);
+}
+
+// src/vkblas_hipblas.c:893-955
+SHIM_EXPORT rocblas_status rocblas_gemm_strided_batched_ex(
+    rocblas_handle handle, rocblas_operation transA, rocblas_operation transB, rocblas_int m,
+    rocblas_int n, rocblas_int k, const void* alpha, const void* a, rocblas_datatype a_type,
+    rocblas_int lda, int64_t strideA, const void* b, rocblas_datatype b_type, rocblas_int ldb,
+    int64_t strideB, const void* beta, const void* c, rocblas_datatype c_type, rocblas_int ldc,
+    int64_t strideC, void* d, rocblas_datatype d_type, rocblas_int ldd, int64_t strideD,
+    rocblas_int batch_count, rocblas_datatype compute_type, rocblas_gemm_algo algo,
+    int32_t solution_index, uint32_t flags) {
+    ShimHandle* h = as_roc(handle);
+    if (!h) return rocblas_status_invalid_value;
+    if (m <= 0 || n <= 0 || k <= 0 || batch_count <= 0) return rocblas_status_invalid_value;
+    int dt = roc_dtype(a_type, b_type, c_type, d_type);
+    if (c == d && ldc == ldd && compute_type == rocblas_datatype_f32_r && dt >= 0) {
+        Run r = run_gemm(h, (vkblas_dtype_t)dt, roc_to_hip_op(transA), roc_to_hip_op(transB), m, n,
+                         k, alpha, a, lda, strideA, b, ldb, strideB, beta, d, ldd, strideC,
+                         batch_count, false);
+        if (r == Run::Done) return rocblas_status_success;
+        if (r == Run::Invalid) return rocblas_status_invalid_value;
+    }
+    return FWD_RC(rocblas_gemm_strided_batched_ex, handle, transA, transB, m, n, k, alpha, a,
+                  a_type, lda, strideA, b, b_type, ldb, strideB, beta, c, c_type, ldc, strideC, d,
+                  d_type, ldd, strideD, batch_count, compute_type, algo, solution_index, flags);
+}
