@@ -130,7 +130,7 @@ def test_rocblas_rules_without_device_work():
 def test_engine_validation_and_no_device():
     p = 0x10000
     assert vk.gemm(vk.DT_F32, 0, 0, 0, 4, 4, 1.0, p, 4, p, 4, 0.0, p, 4) == vk.VKBLAS_ERR_PARAM
-    assert vk.gemm(vk.DT_F16, 0, 0, 4, 4, 4, 1.0, p, 2, p, 4, 0.0, p, 4) == vk.VKBLAS_ERR_PARAM
+    assert vk.gemm(vk.DT_F16, 0, 0, 4, 4, 4, 1.0, p, 4, p, 4, 0.0, p, 4, 2, -1, 0, 0) == vk.VKBLAS_ERR_PARAM
     assert vk.gemm(vk.DT_F32, 0, 0, 4, 4, 4, 1.0, 0, 4, p, 4, 0.0, p, 4) == vk.VKBLAS_ERR_PARAM
     assert vk.lib.vkblas_gemm_c64(0, 0, 4, 4, 4, C.c_float(1), C.c_float(0), None, 4, None, 4,
                                   C.c_float(0), C.c_float(0), None, 4, 1, 0, 0, 0) != 0

@@ -1,0 +1,103 @@
+"""tcgen05 tensor-core GEMM (forced path) against the double-precision oracle.
+
+fp16 / bf16 (kind::f16, fp32 accumulate, RNE store): relative Frobenius error
+<= 2e-3 (fp16) / 8e-3 (bf16, 8-bit mantissa output); fp32 (3xTF32):
+<= 1e-5.  Every op combination, ragged M/N/K, alpha/beta, strided batches with
+a broadcast operand, and a C with ldc > N whose padding must stay untouched.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+import vkblas_b200 as vk  # noqa: E402
+from oracle import oracle as orc  # noqa: E402
+from gpu_util import dev, host, dev_u16, host_u16, check_status  # noqa: E402
+
+SHAPES = [
+    (128, 256, 64),       # one tile, one k-block
+    (256, 512, 320),      # several tiles, ragged k-block count
+    (200, 300, 136),      # ragged M, N, K
+    (64, 48, 1000),       # partial tiles, long K
+    (1024, 768, 512),     # many tiles (persistent loop, accumulator double-buffer)
+]
+TOL = {vk.DT_F16: 2e-3, vk.DT_BF16: 8e-3, vk.DT_F32: 1e-5}
+
+
+def _mk(dtype, rng, n):
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    if dtype == vk.DT_F32:
+        return x, None
+    bits = orc.narrow(1 if dtype == vk.DT_BF16 else 0, x)
+    return orc.widen(1 if dtype == vk.DT_BF16 else 0, bits), bits
+
+
+def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8):
+    import torch
+    rng = np.random.default_rng(M * 7 + N * 3 + K + op_a * 2 + op_b + dtype * 11 + batch)
+    lda = (M if op_a else K)
+    ldb = (K if op_b else N)
+    if dtype != vk.DT_F32:      # 16-byte multiples for TMA
+        lda = (lda + 7) // 8 * 8
+        ldb = (ldb + 7) // 8 * 8
+    else:
+        lda += 1                # fp32 accepts any ld (the split pre-pass compacts)
+        ldb += 3
+    ldc = N + ldc_pad
+    rows_a = K if op_a else M
+    rows_b = N if op_b else K
+    sa = 0 if bcast == "a" else rows_a * lda
+    sb = 0 if bcast == "b" else rows_b * ldb
+    sc = M * ldc
+    na = (sa * (batch - 1) if sa else 0) + rows_a * lda
+    nb = (sb * (batch - 1) if sb else 0) + rows_b * ldb
+    nc = sc * (batch - 1) + M * ldc
+    Af, Ab = _mk(dtype, rng, na)
+    Bf, Bb = _mk(dtype, rng, nb)
+    Cf, Cb = _mk(dtype, rng, nc)
+    dt16 = 1 if dtype == vk.DT_BF16 else 0
+    if dtype == vk.DT_F32:
+        dA, dB, dC = dev(Af), dev(Bf), dev(Cf)
+    else:
+        dA, dB, dC = dev_u16(Ab, dt16), dev_u16(Bb, dt16), dev_u16(Cb, dt16)
+    vk.set_path(vk.PATH_TC)
+    try:
+        vk.set_stream(torch.cuda.current_stream())
+        st = vk.gemm(dtype, op_a, op_b, M, N, K, alpha, dA.data_ptr(), lda, dB.data_ptr(), ldb,
+                     beta, dC.data_ptr(), ldc, batch, sa, sb, sc)
+        torch.cuda.synchronize()
+    finally:
+        vk.set_path(vk.PATH_AUTO)
+    assert st == vk.VKBLAS_OK, f"status {st}"
+    assert vk.last_path() == vk.PATH_TC
+    check_status()
+    got = host(dC) if dtype == vk.DT_F32 else orc.widen(dt16, host_u16(dC))
+    want = orc.gemm_rowmajor_f64(op_a, op_b, M, N, K, alpha, np.ascontiguousarray(Af), lda,
+                                 np.ascontiguousarray(Bf), ldb, beta, np.ascontiguousarray(Cf), ldc,
+                                 batch, sa, sb, sc)
+    for bi in range(batch):
+        g = got[bi * sc: bi * sc + M * ldc].reshape(M, ldc)
+        err = orc.rel_frobenius(g[:, :N], want[bi])
+        assert err <= TOL[dtype], f"batch {bi}: relative error {err}"
+        pad = g[:, N:]
+        c0 = Cf[bi * sc: bi * sc + M * ldc].reshape(M, ldc)[:, N:]
+        np.testing.assert_array_equal(pad, c0)
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_BF16, vk.DT_F32], ids=["f16", "bf16", "f32"])
+@pytest.mark.parametrize("ops", [(0, 0), (0, 1), (1, 0), (1, 1)], ids=["NN", "NT", "TN", "TT"])
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"{m}x{n}x{k}" for m, n, k in SHAPES])
+def test_tc_gemm(dtype, ops, shape, cuda):
+    M, N, K = shape
+    _run(dtype, ops[0], ops[1], M, N, K, 1.0, 0.0)
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_BF16, vk.DT_F32], ids=["f16", "bf16", "f32"])
+def test_tc_alpha_beta(dtype, cuda):
+    _run(dtype, 0, 1, 192, 320, 256, 0.75, -0.5)
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_F32], ids=["f16", "f32"])
+@pytest.mark.parametrize("bcast", [None, "a", "b"])
+def test_tc_batched(dtype, bcast, cuda):
+    _run(dtype, 0, 0, 160, 136, 96, 1.0, 0.5, batch=3, bcast=bcast)

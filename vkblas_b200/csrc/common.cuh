@@ -76,7 +76,11 @@ int gemv_auto_splitk(const GemmProblem& p, int num_sms);
 size_t gemv_workspace_bytes(const GemmProblem& p, int splitk);
 cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaStream_t s);
 bool umma_supported(const GemmProblem& p);
-cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, cudaStream_t s);
+bool umma_profitable(const GemmProblem& p);
+size_t umma_workspace_bytes(const GemmProblem& p);
+// cudaErrorNotSupported: the operands cannot be described to TMA (nothing launched).
+cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* workspace,
+                             cudaStream_t s);
 // Host-side launch counter (all kernels of this library).
 void count_launch();
 }  // namespace vkb

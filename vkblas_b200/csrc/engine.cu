@@ -73,7 +73,8 @@ struct DeviceState {
     int cc_major = 0, cc_minor = 0;
     int* d_status = nullptr;
     std::mutex mu;
-    std::unordered_map<cudaStream_t, Workspace> ws;
+    // [0]: GEMV split-K (partials + zero-initialised tickets), [1]: 3xTF32 operand planes.
+    std::unordered_map<cudaStream_t, Workspace> ws[2];
 };
 
 std::mutex g_dev_mu;
@@ -98,14 +99,14 @@ DeviceState* device_state(int dev) {
     return d;
 }
 
-// Grow-only scratch per (device, stream).  Growth frees the old buffer
+// Grow-only scratch per (device, kind, stream).  Growth frees the old buffer
 // (cudaFree waits for the device) and zero-fills the new one on the stream,
 // which is what the GEMV split-K tickets need.  Not callable during stream
 // capture: make one call of the largest shape before capturing.
-void* workspace(DeviceState* ds, cudaStream_t s, size_t bytes) {
+void* workspace(DeviceState* ds, int kind, cudaStream_t s, size_t bytes) {
     if (bytes == 0) return nullptr;
     std::lock_guard<std::mutex> lk(ds->mu);
-    Workspace& w = ds->ws[s];
+    Workspace& w = ds->ws[kind][s];
     if (w.bytes >= bytes) return w.ptr;
     if (w.ptr) cudaFree(w.ptr);
     w.ptr = nullptr;
@@ -142,11 +143,10 @@ const char* path_name(int p) {
 vkblas_status_t check_problem(const GemmProblem& p) {
     if (p.M == 0 || p.N == 0 || p.K == 0 || p.batch == 0) return VKBLAS_ERR_PARAM;
     if (!p.A || !p.B || !p.C) return VKBLAS_ERR_PARAM;
-    // Leading dimensions must cover a row of the stored matrix (the bound
-    // hipBLAS itself enforces: lda >= rows of the column-major operand).
-    if (p.lda < (p.op_a ? p.M : p.K)) return VKBLAS_ERR_PARAM;
-    if (p.ldb < (p.op_b ? p.K : p.N)) return VKBLAS_ERR_PARAM;
-    if (p.ldc < p.N) return VKBLAS_ERR_PARAM;
+    // Like the reference engine (src/vkblas.c:3114, 3528), leading dimensions
+    // are not checked against the matrix extents: a smaller ld makes rows
+    // overlap, which the reference's own tests use (test/test_h.c:105 with
+    // op_a == T) and which the SIMT kernel computes exactly as addressed.
     if (p.sa < 0 || p.sb < 0 || p.sc < 0) return VKBLAS_ERR_PARAM;
     return VKBLAS_OK;
 }
@@ -169,8 +169,8 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
         if (gemv_supported(p)) path = VKBLAS_PATH_GEMV;
     }
     if (!path && (forced == VKBLAS_PATH_AUTO || forced == VKBLAS_PATH_TC)) {
-        bool allow = forced == VKBLAS_PATH_TC ||
-                     (p.dtype == DT_F32 ? cfg.sgemm != 1 : cfg.hgemm != 1);
+        const int mode = p.dtype == DT_F32 ? cfg.sgemm : cfg.hgemm;   // 0 auto, 1 simt, 2 tc
+        bool allow = forced == VKBLAS_PATH_TC || mode == 2 || (mode == 0 && umma_profitable(p));
         if (allow && umma_supported(p)) path = VKBLAS_PATH_TC;
     }
     if (!path && (forced == VKBLAS_PATH_AUTO || forced == VKBLAS_PATH_SIMT)) path = VKBLAS_PATH_SIMT;
@@ -185,12 +185,22 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
         void* ws = nullptr;
         size_t need = gemv_workspace_bytes(p, splitk);
         if (need) {
-            ws = workspace(ds, s, need);
+            ws = workspace(ds, 0, s, need);
             if (!ws) splitk = 1;
         }
         e = launch_gemv(p, splitk, ws, s);
     } else if (path == VKBLAS_PATH_TC) {
-        e = launch_umma_gemm(p, ds->num_sms, ds->d_status, s);
+        const size_t need = umma_workspace_bytes(p);
+        void* ws = need ? workspace(ds, 1, s, need) : nullptr;
+        e = (need && !ws) ? cudaErrorNotSupported : launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, s);
+        if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
+            cudaGetLastError();
+            path = VKBLAS_PATH_SIMT;       // operands TMA cannot describe: exact SIMT path
+            e = launch_simt_gemm(p, s);
+        } else if (e == cudaErrorNotSupported) {
+            cudaGetLastError();
+            return VKBLAS_ERR_FALLBACK;
+        }
     } else {
         e = launch_simt_gemm(p, s);
     }

@@ -1,9 +1,711 @@
-// umma_gemm.cu -- tcgen05 GEMM (placeholder until the tensor-core kernels land).
+// umma_gemm.cu -- tcgen05 (5th-gen tensor core) GEMM for sm_100a.
+//
+// Replaces the reference's tile shaders for the large-GEMM path (lakitu12/vkblas
+// src/shaders/gemm_half_128x128_bankfree_tmpl.comp, gemm_f32_128x128_bankfree_tmpl.comp
+// and their 64x64 / 128x256 / split-K variants, dispatched from
+// src/vkblas.c:1550-1756 and 2810-2884).  Same contract: row-major
+// C = alpha*op(A)*op(B) + beta*C per batch entry, fp32 accumulation, fp32
+// epilogue with C unread when beta == 0, RNE store for 2-byte outputs.
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: SWIZZLE_128B tiles of A and B into a STAGES-deep
+//               shared-memory ring (full/empty mbarrier pairs).  op(A)/op(B)
+//               are absorbed here: a K-major operand is loaded as rows of 128
+//               bytes of K, an MN-major one as 128-byte slabs of M (or N) per
+//               k-row, and the UMMA descriptors say which (no transpose pass,
+//               unlike the reference's transpose shaders, src/vkblas.c:970-1188).
+//   warp 1      allocates TMEM (two accumulators, double-buffered across
+//               tiles) and issues tcgen05.mma from one thread; tcgen05.commit
+//               releases smem stages and hands finished accumulators over.
+//   warps 2-5   epilogue (2-9 for 3xTF32): tcgen05.ld (32 lanes x 32 columns
+//               per step) -> alpha/beta -> convert -> global, overlapping the
+//               next tile's main loop.
+//
+// fp32 (3xTF32, after Ootomo & Yokota 2022, "Recovering single precision
+// accuracy from Tensor Cores while surpassing the FP32 theoretical peak
+// performance"): a pre-pass splits each operand x into big = tf32(x) and
+// small = tf32(x - big) (both round-to-nearest-even, low 13 bits zero, written
+// as compact K-major planes in a workspace -- an MN-major operand is
+// transposed on the way, the tf32 MMAs only ever read K-major tiles) and the
+// main loop accumulates A_small*B_big + A_big*B_small + A_big*B_big into one
+// fp32 TMEM accumulator.
+//
+// No cluster multicast anywhere: each CTA issues its own TMA loads.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace vkb {
-bool umma_supported(const GemmProblem&) { return false; }
-cudaError_t launch_umma_gemm(const GemmProblem&, int, int*, cudaStream_t) {
-    return cudaErrorNotSupported;
+namespace {
+
+using namespace umma;
+
+enum Kind : int { K_F16 = 0, K_BF16 = 1, K_TF32X3 = 2 };
+
+constexpr int BM = 128;
+constexpr uint32_t ROW_BYTES = 128;       // one SWIZZLE_128B atom row
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;
+
+struct __align__(64) UmmaParams {
+    CUtensorMap tmA[2];          // [plane]; 2-byte kinds use plane 0, 3xTF32 big / small
+    CUtensorMap tmB[2];
+    void* C;
+    uint32_t ldc;
+    int64_t sc;
+    uint32_t M, N, K, batch;
+    uint32_t tiles_m, tiles_n, num_kb, total_tiles;
+    uint32_t a_batched, b_batched;
+    float alpha, beta;
+    const float* d_alpha;
+    const float* d_beta;
+    int* status;
+    uint32_t c_vec_ok;
+};
+
+template <int KIND> struct OutT;
+template <> struct OutT<K_F16> { using T = __half; };
+template <> struct OutT<K_BF16> { using T = __nv_bfloat16; };
+template <> struct OutT<K_TF32X3> { using T = float; };
+
+__device__ __forceinline__ void tile_coords(const UmmaParams& p, uint32_t t, uint32_t& b,
+                                            uint32_t& mb, uint32_t& nb) {
+    const uint32_t per = p.tiles_m * p.tiles_n;
+    b = t / per;
+    const uint32_t r = t - b * per;
+    // Groups of 8 M-blocks sweep the N-blocks together: consecutive tiles
+    // (which run concurrently on neighbouring SMs) share A rows and B columns in L2.
+    const uint32_t G = 8;
+    const uint32_t group = r / (G * p.tiles_n);
+    const uint32_t first_m = group * G;
+    const uint32_t gsize = min(p.tiles_m - first_m, G);
+    const uint32_t in = r - group * G * p.tiles_n;
+    mb = first_m + in % gsize;
+    nb = in / gsize;
 }
+
+// Epilogue of 32 consecutive outputs of one row: C = alpha*v + beta*C (C not
+// read when beta == 0), converted to T; 128-bit accesses when aligned.
+template <typename T>
+__device__ __forceinline__ void store_row32(T* crow, const float (&v)[32], uint32_t ncols,
+                                            bool vec, float alpha, float beta) {
+    if (vec && ncols == 32) {
+        if constexpr (sizeof(T) == 2) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                uint4 old = make_uint4(0, 0, 0, 0);
+                if (beta != 0.f) old = *reinterpret_cast<const uint4*>(crow + q * 8);
+                const T* o = reinterpret_cast<const T*>(&old);
+                uint4 out;
+                T* w = reinterpret_cast<T*>(&out);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float c = (beta != 0.f) ? Elem<T>::to_f(o[i]) : 0.f;
+                    w[i] = Elem<T>::from_f(epilogue(alpha, v[q * 8 + i], beta, c));
+                }
+                *reinterpret_cast<uint4*>(crow + q * 8) = out;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (beta != 0.f) old = *reinterpret_cast<const float4*>(crow + q * 4);
+                float4 out;
+                out.x = epilogue(alpha, v[q * 4 + 0], beta, old.x);
+                out.y = epilogue(alpha, v[q * 4 + 1], beta, old.y);
+                out.z = epilogue(alpha, v[q * 4 + 2], beta, old.z);
+                out.w = epilogue(alpha, v[q * 4 + 3], beta, old.w);
+                *reinterpret_cast<float4*>(crow + q * 4) = out;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            if ((uint32_t)i < ncols) {
+                const float c = (beta != 0.f) ? Elem<T>::to_f(crow[i]) : 0.f;
+                crow[i] = Elem<T>::from_f(epilogue(alpha, v[i], beta, c));
+            }
+        }
+    }
+}
+
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES>
+struct Cfg {
+    static constexpr int E = (KIND == K_TF32X3) ? 4 : 2;
+    static constexpr int PLANES = (KIND == K_TF32X3) ? 2 : 1;
+    static constexpr int BK = ROW_BYTES / E;          // K elements per stage (64 or 32)
+    static constexpr int UK = 32 / E;                 // K per UMMA instruction (16 or 8)
+    static constexpr int KSTEPS = BK / UK;            // 4
+    static constexpr int EPB = ROW_BYTES / E;         // elements per 128-byte MN slab
+    static constexpr uint32_t A_PLANE = BM * ROW_BYTES;
+    static constexpr uint32_t B_PLANE = BN * ROW_BYTES;
+    static constexpr uint32_t STAGE_BYTES = PLANES * (A_PLANE + B_PLANE);
+    // The tensor core's fp32 accumulation truncates, so its error grows
+    // linearly with the number of accumulating MMAs (measured on B200: relative
+    // error ~7e-9 * K, biased toward zero).  3xTF32 therefore accumulates each
+    // SEG_KB-block K segment in a fresh TMEM buffer and the epilogue adds the
+    // segments in fp32 with round-to-nearest; 2-byte kinds keep one
+    // accumulator per tile (their tolerance is far above that error).
+    static constexpr uint32_t SEG_KB = (KIND == K_TF32X3) ? 8u : 0u;
+    static constexpr uint32_t NBUF = SEG_KB ? 4u : 2u;            // TMEM accumulator buffers
+    // Epilogue warps: 4 (one per TMEM lane quarter), or 8 for the segmented
+    // epilogue, where two warps share a quarter and each keeps the fp32 sums of
+    // half of the tile's columns in registers.
+    static constexpr int EPI_WARPS = SEG_KB ? 8 : 4;
+    static constexpr int EPI_COLS = BN * 4 / EPI_WARPS;          // columns per epilogue thread
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr uint32_t TMEM_COLS = NBUF * BN;                // 512
+    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr uint32_t IDESC =
+        instr_desc(KIND == K_F16 ? 0u : KIND == K_BF16 ? 1u : 2u, A_MN, B_MN, BM, BN);
+    static constexpr uint32_t SLAB = BK * ROW_BYTES;  // MN-major: one 128-byte-wide slab
+    static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
+    static_assert(SEG_KB == 0 || EPI_COLS <= 64, "segmented epilogue keeps EPI_COLS fp32 sums per thread");
+};
+
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES>
+__global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
+    umma_gemm_kernel(const __grid_constant__ UmmaParams p) {
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES>;
+    using TOut = typename OutT<KIND>::T;
+    constexpr uint32_t NBUF = C_::NBUF;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    const uint32_t pad = (1024u - (raw_base & 1023u)) & 1023u;
+    uint8_t* smem = smem_raw + pad;
+    const uint32_t sbase = raw_base + pad;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](uint32_t a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](uint32_t a) { return bar0 + 8u * (2 * STAGES + NBUF + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 2 * NBUF);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * NBUF + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    // K segments per tile (one when the accumulator is not segmented).
+    const uint32_t seg_kb = C_::SEG_KB ? C_::SEG_KB : p.num_kb;
+    const uint32_t nseg = (p.num_kb + seg_kb - 1) / seg_kb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (uint32_t a = 0; a < NBUF; a++) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 32 * C_::EPI_WARPS);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&p.tmA[0]);
+        prefetch_tmap(&p.tmB[0]);
+        if (C_::PLANES == 2) {
+            prefetch_tmap(&p.tmA[1]);
+            prefetch_tmap(&p.tmB[1]);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C_::TMEM_COLS);
+        tmem_relinquish();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_mask = 0, issued_parity = 0;   // per stage: issued ever / last parity
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+                uint32_t b, mb, nb;
+                tile_coords(p, t, b, mb, nb);
+                const int32_t m0 = (int32_t)(mb * BM), n0 = (int32_t)(nb * BN);
+                const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
+                for (uint32_t kb = 0; kb < p.num_kb; kb++) {
+                    if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
+                                  DS_TIMEOUT_PRODUCER, WAIT_LIMIT_NS)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full_bar(stage);
+                    mbar_arrive_expect_tx(fb, C_::STAGE_BYTES);
+                    const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
+                    const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
+                    const int32_t k0 = (int32_t)(kb * C_::BK);
+#pragma unroll
+                    for (int pl = 0; pl < C_::PLANES; pl++) {
+                        if (!A_MN) {
+                            tma_load_3d(sA + pl * C_::A_PLANE, &p.tmA[pl], fb, k0, m0, ba);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < BM / C_::EPB; j++)
+                                tma_load_3d(sA + pl * C_::A_PLANE + j * C_::SLAB, &p.tmA[pl], fb,
+                                            m0 + j * C_::EPB, k0, ba);
+                        }
+                        if (!B_MN) {
+                            tma_load_3d(sB + pl * C_::B_PLANE, &p.tmB[pl], fb, k0, n0, bb);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < BN / C_::EPB; j++)
+                                tma_load_3d(sB + pl * C_::B_PLANE + j * C_::SLAB, &p.tmB[pl], fb,
+                                            n0 + j * C_::EPB, k0, bb);
+                        }
+                    }
+                    issued_mask |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Never leave with copies in flight: wait for the last fill of every stage.
+            for (int s = 0; s < STAGES; s++)
+                if (issued_mask & (1u << s))
+                    drain_bar_wait(full_bar(s), (issued_parity >> s) & 1u, p.status,
+                                   DS_TIMEOUT_PRODUCER, DRAIN_LIMIT_NS);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, u = 0;          // u: accumulator hand-overs so far
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+                for (uint32_t sg = 0; ok && sg < nseg; sg++, u++) {
+                    const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
+                    if (!wait_bar(tempty_bar(buf), bph ^ 1u, abort_flag, p.status, DS_TIMEOUT_MMA,
+                                  WAIT_LIMIT_NS)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + buf * BN;
+                    const uint32_t kb0 = sg * seg_kb;
+                    const uint32_t kb1 = min(p.num_kb, kb0 + seg_kb);
+                    for (uint32_t kb = kb0; kb < kb1; kb++) {
+                        if (!wait_bar(full_bar(stage), phase, abort_flag, p.status, DS_TIMEOUT_MMA,
+                                      WAIT_LIMIT_NS)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
+                        const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
+#pragma unroll
+                        for (int j = 0; j < C_::KSTEPS; j++) {
+                            uint64_t ad[C_::PLANES], bd[C_::PLANES];
+#pragma unroll
+                            for (int pl = 0; pl < C_::PLANES; pl++) {
+                                ad[pl] = A_MN ? smem_desc_sw128(sA + pl * C_::A_PLANE + j * C_::UK * ROW_BYTES,
+                                                                C_::SLAB, 1024)
+                                              : smem_desc_sw128(sA + pl * C_::A_PLANE + j * 32, 16, 1024);
+                                bd[pl] = B_MN ? smem_desc_sw128(sB + pl * C_::B_PLANE + j * C_::UK * ROW_BYTES,
+                                                                C_::SLAB, 1024)
+                                              : smem_desc_sw128(sB + pl * C_::B_PLANE + j * 32, 16, 1024);
+                            }
+                            const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
+                            if constexpr (KIND == K_TF32X3) {
+                                mma_tf32(d, ad[1], bd[0], C_::IDESC, first);   // A_small * B_big
+                                mma_tf32(d, ad[0], bd[1], C_::IDESC, 1u);      // A_big * B_small
+                                mma_tf32(d, ad[0], bd[0], C_::IDESC, 1u);      // A_big * B_big
+                            } else {
+                                mma_f16(d, ad[0], bd[0], C_::IDESC, first);
+                            }
+                        }
+                        tc_commit(empty_bar(stage));
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    tc_commit(tfull_bar(buf));
+                }
+            }
+            // Never leave with MMAs in flight.
+            tc_commit(drain_bar);
+            drain_bar_wait(drain_bar, 0, p.status, DS_TIMEOUT_MMA, DRAIN_LIMIT_NS);
+        }
+    } else {
+        // --------------------------------------------------------- epilogue
+        float alpha = p.alpha, beta = p.beta;
+        load_scalars(p.d_alpha, p.d_beta, alpha, beta);
+        const uint32_t q = (uint32_t)(warp & 3);          // TMEM lane quarter of this warp
+        const uint32_t col0 = (uint32_t)((warp - 2) / 4) * C_::EPI_COLS;   // this warp's columns
+        const uint32_t row = q * 32u + (uint32_t)lane;
+        const uint32_t lane_off = (q * 32u) << 16;
+        TOut* Cbase = reinterpret_cast<TOut*>(p.C);
+        uint32_t u = 0;
+        bool ok = true;
+        for (uint32_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+            uint32_t b, mb, nb;
+            tile_coords(p, t, b, mb, nb);
+            const uint32_t m = mb * BM + row;
+            TOut* crow = Cbase + p.sc * (int64_t)b + (size_t)m * p.ldc;
+            if constexpr (C_::SEG_KB == 0) {
+                const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
+                ok = wait_bar(tfull_bar(buf), bph, abort_flag, p.status, DS_TIMEOUT_EPILOGUE,
+                              WAIT_LIMIT_NS);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < C_::EPI_COLS / 32; c++) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tmem_base + lane_off + buf * BN + col0 + c * 32, r);
+                    tmem_wait_ld();
+                    const uint32_t n0 = nb * BN + col0 + c * 32;
+                    if (m < p.M && n0 < p.N)
+                        store_row32<TOut>(crow + n0, reinterpret_cast<const float(&)[32]>(r),
+                                          min(32u, p.N - n0), p.c_vec_ok != 0, alpha, beta);
+                }
+                tc_fence_before();
+                mbar_arrive(tempty_bar(buf));
+                u++;
+            } else {
+                float sum[C_::EPI_COLS / 32][32];
+                for (uint32_t sg = 0; sg < nseg; sg++, u++) {
+                    const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
+                    ok = wait_bar(tfull_bar(buf), bph, abort_flag, p.status, DS_TIMEOUT_EPILOGUE,
+                                  WAIT_LIMIT_NS);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < C_::EPI_COLS / 32; c++) {
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(tmem_base + lane_off + buf * BN + col0 + c * 32, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            sum[c][i] = sg ? __fadd_rn(sum[c][i], __uint_as_float(r[i]))
+                                           : __uint_as_float(r[i]);
+                    }
+                    tc_fence_before();
+                    mbar_arrive(tempty_bar(buf));
+                }
+                if (!ok) break;
+#pragma unroll
+                for (int c = 0; c < C_::EPI_COLS / 32; c++) {
+                    const uint32_t n0 = nb * BN + col0 + c * 32;
+                    if (m < p.M && n0 < p.N)
+                        store_row32<TOut>(crow + n0, sum[c], min(32u, p.N - n0), p.c_vec_ok != 0,
+                                          alpha, beta);
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C_::TMEM_COLS);
+    }
+}
+
+// 3xTF32 pre-pass: x -> big = rn_tf32(x), small = rn_tf32(x - big), written as
+// compact [nb][rows][ldo] planes (ldo = cols rounded up to 4, pad columns zero).
+__device__ __forceinline__ float rn_tf32(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7F800000u) == 0x7F800000u) return x;               // inf / nan unchanged
+    u += 0xFFFu + ((u >> 13) & 1u);
+    return __uint_as_float(u & 0xFFFFE000u);
+}
+
+__global__ void split_tf32_kernel(const float* __restrict__ src, uint32_t rows, uint32_t cols,
+                                  uint32_t ld, int64_t bstride, uint32_t nb, uint32_t ldo,
+                                  float* __restrict__ big, float* __restrict__ small) {
+    const uint64_t total = (uint64_t)nb * rows * (ldo / 4);
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t br = i / (ldo / 4);
+        const uint32_t c0 = (uint32_t)(i - br * (ldo / 4)) * 4u;
+        const uint32_t b = (uint32_t)(br / rows), r = (uint32_t)(br - (uint64_t)b * rows);
+        const float* s = src + bstride * (int64_t)b + (size_t)r * ld;
+        float x[4], hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) x[j] = (c0 + j < cols) ? __ldg(s + c0 + j) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            hi[j] = rn_tf32(x[j]);
+            const float d = x[j] - hi[j];
+            lo[j] = isfinite(hi[j]) ? rn_tf32(d) : 0.f;
+        }
+        const uint64_t o = br * ldo + c0;
+        *reinterpret_cast<float4*>(big + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(small + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// Same split for an MN-major operand (src[b][k][ld], MN contiguous), written
+// K-major (out[b][mn][ldo], K contiguous) through a 32x32 shared-memory tile,
+// so that the tf32 MMAs always read K-major operands.
+__global__ void split_tf32_t_kernel(const float* __restrict__ src, uint32_t K, uint32_t MN,
+                                    uint32_t ld, int64_t bstride, uint32_t nb, uint32_t ldo,
+                                    float* __restrict__ big, float* __restrict__ small) {
+    __shared__ float tile[32][33];
+    const uint32_t mn0 = blockIdx.x * 32u, k0 = blockIdx.y * 32u;
+    for (uint32_t b = blockIdx.z; b < nb; b += gridDim.z) {
+        const float* s = src + bstride * (int64_t)b;
+        for (uint32_t i = threadIdx.y; i < 32u; i += 8u) {
+            const uint32_t k = k0 + i, mn = mn0 + threadIdx.x;
+            tile[i][threadIdx.x] = (k < K && mn < MN) ? __ldg(s + (size_t)k * ld + mn) : 0.f;
+        }
+        __syncthreads();
+        const size_t obase = (size_t)b * MN * ldo;
+        for (uint32_t i = threadIdx.y; i < 32u; i += 8u) {
+            const uint32_t mn = mn0 + i, k = k0 + threadIdx.x;
+            if (mn < MN && k < ldo) {
+                const float x = tile[threadIdx.x][i];
+                const float hi = rn_tf32(x);
+                const float lo = isfinite(hi) ? rn_tf32(x - hi) : 0.f;
+                big[obase + (size_t)mn * ldo + k] = hi;
+                small[obase + (size_t)mn * ldo + k] = lo;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ----------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// 3-D map over [nbatch][outer][inner] with element strides ld / bstride.
+bool make_tmap(CUtensorMap* m, CUtensorMapDataType dt, uint32_t esize, const void* base,
+               uint64_t inner, uint64_t outer, uint64_t ld, uint64_t nbatch, uint64_t bstride,
+               uint32_t box_inner, uint32_t box_outer) {
+    auto enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {inner, outer, nbatch};
+    cuuint64_t strides[2] = {ld * esize, (nbatch > 1 ? bstride : outer * ld) * esize};
+    cuuint32_t box[3] = {box_inner, box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline uint32_t rup4(uint32_t x) { return (x + 3u) & ~3u; }
+
+struct Operand {      // one operand as the tensor maps see it
+    const void* base;
+    uint64_t inner, outer, ld, nb, bstride;
+    bool mn_major;
+};
+
+Operand operand_a(const GemmProblem& p) {
+    Operand o;
+    o.base = p.A;
+    o.mn_major = p.op_a != 0;                       // A[k*lda + m]
+    o.inner = o.mn_major ? p.M : p.K;
+    o.outer = o.mn_major ? p.K : p.M;
+    o.ld = p.lda;
+    o.nb = (p.batch > 1 && p.sa != 0) ? p.batch : 1;
+    o.bstride = (uint64_t)p.sa;
+    return o;
+}
+Operand operand_b(const GemmProblem& p) {
+    Operand o;
+    o.base = p.B;
+    o.mn_major = p.op_b == 0;                       // B[k*ldb + n]
+    o.inner = o.mn_major ? p.N : p.K;
+    o.outer = o.mn_major ? p.K : p.N;
+    o.ld = p.ldb;
+    o.nb = (p.batch > 1 && p.sb != 0) ? p.batch : 1;
+    o.bstride = (uint64_t)p.sb;
+    return o;
+}
+
+bool tma_ok_16bit(const Operand& o) {
+    if (!al16(o.base) || (o.ld * 2) % 16 != 0 || o.ld < o.inner) return false;
+    if (o.nb > 1 && ((o.bstride * 2) % 16 != 0 || o.bstride < o.outer * o.ld)) return false;
+    return o.inner < (1ull << 32) && o.outer < (1ull << 31);
+}
+
+// 3xTF32 planes are always K-major: rows = the operand's M (or N), cols = K.
+uint64_t plane_rows(const Operand& o) { return o.mn_major ? o.inner : o.outer; }
+uint32_t plane_k(const Operand& o) { return (uint32_t)(o.mn_major ? o.outer : o.inner); }
+uint64_t plane_elems(const Operand& o) { return o.nb * plane_rows(o) * rup4(plane_k(o)); }
+
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES>
+cudaError_t launch_kind(const UmmaParams& prm, int grid, cudaStream_t s) {
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES>;
+    auto kern = umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES>;
+    static std::atomic<uint64_t> attr_done{0};     // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_done.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)C_::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_done.fetch_or(bit);
+    }
+    kern<<<grid, C_::THREADS, C_::SMEM_BYTES, s>>>(prm);
+    count_launch();
+    return cudaGetLastError();
+}
+
+template <int KIND, int BN, int STAGES>
+cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, int grid, cudaStream_t s) {
+    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES>(prm, grid, s);
+    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES>(prm, grid, s);
+    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES>(prm, grid, s);
+    return launch_kind<KIND, true, true, BN, STAGES>(prm, grid, s);
+}
+
+constexpr int BN_16 = 256, STAGES_16 = 4;
+constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
+
+}  // namespace
+
+bool umma_supported(const GemmProblem& p) {
+    if (!encode_fn()) return false;
+    if (p.dtype == DT_F16 || p.dtype == DT_BF16)
+        return tma_ok_16bit(operand_a(p)) && tma_ok_16bit(operand_b(p));
+    if (p.dtype == DT_F32) {
+        Operand a = operand_a(p), b = operand_b(p);
+        return a.inner < (1ull << 31) && a.outer < (1ull << 21) * 32 && b.inner < (1ull << 31) &&
+               b.outer < (1ull << 21) * 32;
+    }
+    return false;
+}
+
+bool umma_profitable(const GemmProblem& p) {
+    return (uint64_t)p.M * p.N * p.K >= (1ull << 21) && p.M >= 32 && p.N >= 32;
+}
+
+size_t umma_workspace_bytes(const GemmProblem& p) {
+    if (p.dtype != DT_F32) return 0;
+    const uint64_t a = plane_elems(operand_a(p)), b = plane_elems(operand_b(p));
+    // big and small planes of A and B, each 256-byte aligned
+    return (size_t)(2 * ((a * 4 + 255) / 256 * 256) + 2 * ((b * 4 + 255) / 256 * 256));
+}
+
+cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* ws,
+                             cudaStream_t s) {
+    UmmaParams prm;
+    memset(&prm, 0, sizeof(prm));
+    const Operand a = operand_a(p), b = operand_b(p);
+    const bool is32 = p.dtype == DT_F32;
+    const int BN = is32 ? BN_TF32 : BN_16;
+    const uint32_t esize = is32 ? 4u : 2u;
+    const uint32_t BK = ROW_BYTES / esize, EPB = ROW_BYTES / esize;
+
+    auto box_for = [&](const Operand& o, uint32_t tile_rows, uint32_t& bi, uint32_t& bo) {
+        if (o.mn_major) { bi = EPB; bo = BK; }          // 128-byte MN slab x BK k-rows
+        else { bi = BK; bo = tile_rows; }               // BK k (128 bytes) x tile rows
+    };
+    uint32_t abi, abo, bbi, bbo;
+    box_for(a, BM, abi, abo);
+    box_for(b, (uint32_t)BN, bbi, bbo);
+
+    if (!is32) {
+        const CUtensorMapDataType dt =
+            p.dtype == DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        if (!make_tmap(&prm.tmA[0], dt, 2, a.base, a.inner, a.outer, a.ld, a.nb, a.bstride, abi, abo) ||
+            !make_tmap(&prm.tmB[0], dt, 2, b.base, b.inner, b.outer, b.ld, b.nb, b.bstride, bbi, bbo))
+            return cudaErrorNotSupported;
+    } else {
+        if (!ws) return cudaErrorNotSupported;
+        const uint64_t ae = plane_elems(a), be = plane_elems(b);
+        char* w = reinterpret_cast<char*>(ws);
+        float* a_big = reinterpret_cast<float*>(w);
+        w += (ae * 4 + 255) / 256 * 256;
+        float* a_small = reinterpret_cast<float*>(w);
+        w += (ae * 4 + 255) / 256 * 256;
+        float* b_big = reinterpret_cast<float*>(w);
+        w += (be * 4 + 255) / 256 * 256;
+        float* b_small = reinterpret_cast<float*>(w);
+        const uint32_t lda_o = rup4(plane_k(a)), ldb_o = rup4(plane_k(b));
+        const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        const uint64_t ar = plane_rows(a), br = plane_rows(b);
+        const uint64_t sa_o = ar * lda_o, sb_o = br * ldb_o;
+        // K-major boxes: BK (32 fp32 = 128 bytes) x tile rows
+        if (!make_tmap(&prm.tmA[0], dt, 4, a_big, plane_k(a), ar, lda_o, a.nb, sa_o, BK, BM) ||
+            !make_tmap(&prm.tmA[1], dt, 4, a_small, plane_k(a), ar, lda_o, a.nb, sa_o, BK, BM) ||
+            !make_tmap(&prm.tmB[0], dt, 4, b_big, plane_k(b), br, ldb_o, b.nb, sb_o, BK, BN) ||
+            !make_tmap(&prm.tmB[1], dt, 4, b_small, plane_k(b), br, ldb_o, b.nb, sb_o, BK, BN))
+            return cudaErrorNotSupported;
+        auto split = [&](const Operand& o, uint32_t ldo, float* big, float* small) {
+            if (!o.mn_major) {
+                const uint64_t work = o.nb * o.outer * (ldo / 4);
+                const int threads = 256;
+                const uint64_t want = (work + threads - 1) / threads;
+                const int blocks = (int)(want < (uint64_t)num_sms * 16 ? want : (uint64_t)num_sms * 16);
+                split_tf32_kernel<<<blocks > 0 ? blocks : 1, threads, 0, s>>>(
+                    reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
+                    (uint32_t)o.ld, (int64_t)o.bstride, (uint32_t)o.nb, ldo, big, small);
+            } else {
+                dim3 grid((uint32_t)((o.inner + 31) / 32), (uint32_t)((o.outer + 31) / 32),
+                          (uint32_t)(o.nb < 65535 ? o.nb : 65535));
+                split_tf32_t_kernel<<<grid, dim3(32, 8), 0, s>>>(
+                    reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
+                    (uint32_t)o.ld, (int64_t)o.bstride, (uint32_t)o.nb, ldo, big, small);
+            }
+            count_launch();
+        };
+        split(a, lda_o, a_big, a_small);
+        split(b, ldb_o, b_big, b_small);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    prm.C = p.C;
+    prm.ldc = p.ldc;
+    prm.sc = p.sc;
+    prm.M = p.M; prm.N = p.N; prm.K = p.K; prm.batch = p.batch;
+    prm.tiles_m = (p.M + BM - 1) / BM;
+    prm.tiles_n = (p.N + BN - 1) / BN;
+    prm.num_kb = (p.K + BK - 1) / BK;
+    const uint64_t total = (uint64_t)prm.tiles_m * prm.tiles_n * p.batch;
+    if (total >= (1ull << 31)) return cudaErrorNotSupported;
+    prm.total_tiles = (uint32_t)total;
+    prm.a_batched = a.nb > 1;
+    prm.b_batched = b.nb > 1;
+    prm.alpha = p.alpha; prm.beta = p.beta; prm.d_alpha = p.d_alpha; prm.d_beta = p.d_beta;
+    prm.status = d_status;
+    prm.c_vec_ok = al16(p.C) && ((uint64_t)p.ldc * esize) % 16 == 0 &&
+                   (p.batch == 1 || ((uint64_t)p.sc * esize) % 16 == 0);
+    const int grid = (int)(total < (uint64_t)num_sms ? total : (uint64_t)num_sms);
+    const bool amn = a.mn_major, bmn = b.mn_major;
+    switch (p.dtype) {
+        case DT_F16: return launch_majors<K_F16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
+        case DT_BF16: return launch_majors<K_BF16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
+        case DT_F32:   // planes are K-major whatever op(A), op(B) are
+            return launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32>(prm, grid, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 }  // namespace vkb
