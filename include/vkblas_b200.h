@@ -35,6 +35,27 @@ vkblas_status_t vkblas_gemm_ex(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op
                                int64_t stride_a, int64_t stride_b, int64_t stride_c,
                                void* stream);
 
+/* Split-K decode GEMV that allocates nothing.  No counterpart in the
+ * reference.  For callers that cannot let a library call cudaMalloc (work
+ * inside a framework's allocator or memory pool, or decode loops where a
+ * device-synchronising cudaFree/cudaMalloc of a growing workspace is not
+ * acceptable).  Computes, for 2-byte dtype (VKBLAS_DT_F16 or VKBLAS_DT_BF16),
+ *     C[m*ldc + n] = alpha * sum_k X[m*ldx + k] * W[n*ldw + k] + beta * C[m*ldc + n]
+ * i.e. vkblas_gemm_f16/bf16(VKBLAS_OP_N, VKBLAS_OP_T, M, N, K, ...) with
+ * batch 1, on `stream` (a cudaStream_t; NULL = legacy default stream), with
+ * the K range split into `splitk` (1..16) segments.  Scratch is a fixed 4 MiB
+ * array inside the library (held by every GPU that loads it until exit):
+ * splitk*M*N*4 must fit in 4 MiB - 16 KiB and N in 4096*64 rows, and
+ * M <= 16, K, ldx, ldw multiples of 8, X and W 16-byte aligned; otherwise
+ * VKBLAS_ERR_PARAM and nothing is enqueued.  All calls on a device share the
+ * array: calls whose kernels overlap on the GPU race (order them on one
+ * stream).  The first call on a device looks the array up
+ * (cudaGetSymbolAddress); make it before any stream capture. */
+vkblas_status_t vkblas_gemv_splitk_noalloc(vkblas_dtype_t dtype, uint32_t M, uint32_t N,
+                                           uint32_t K, float alpha, const void* X, uint32_t ldx,
+                                           const void* W, uint32_t ldw, float beta, void* C,
+                                           uint32_t ldc, uint32_t splitk, void* stream);
+
 /* Stream used by the vkblas_gemm_* calls made from the calling thread
  * (thread-local; default NULL = legacy default stream). */
 void vkblas_set_stream(void* stream);

@@ -52,6 +52,9 @@ def _load() -> C.CDLL:
     lib.vkblas_gemm_ex.argtypes = [i32, i32, i32, u32, u32, u32, vp, vp, i32, vp, u32, vp, u32, vp,
                                    u32, u32, i64, i64, i64, vp]
     lib.vkblas_gemm_ex.restype = i32
+    lib.vkblas_gemv_splitk_noalloc.argtypes = [i32, u32, u32, u32, f32, vp, u32, vp, u32, f32, vp,
+                                               u32, u32, vp]
+    lib.vkblas_gemv_splitk_noalloc.restype = i32
     lib.vkblas_set_stream.argtypes = [vp]
     lib.vkblas_get_stream.restype = vp
     lib.vkblas_b200_set_path.argtypes = [i32]

@@ -20,7 +20,10 @@
 // without shared memory.  Split-K partials go to a workspace; the last CTA of
 // each column block (atomic ticket, no waiting) reduces them in segment
 // order, applies alpha/beta and resets its ticket for the next launch.
+#include <mutex>
+
 #include "common.cuh"
+#include "vkblas_b200.h"
 
 namespace vkb {
 namespace {
@@ -282,3 +285,134 @@ cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaS
 }
 
 }  // namespace vkb
+
+// ---------------------------------------------------------------------------
+// Split-K GEMV with library-owned scratch: vkblas_gemv_splitk_noalloc.
+//
+// Some callers cannot let a library call cudaMalloc: code that runs inside a
+// framework's own memory pool or allocator hook (a nested cudaMalloc there can
+// re-enter the allocator or bypass its accounting), and latency-critical
+// decode loops, where the grow-only workspace behind vkblas_gemm_f16 may free
+// and reallocate when a larger shape appears -- and cudaFree / cudaMalloc
+// synchronise the whole device.  This entry point runs the same split-K GEMV
+// kernel, but its scratch (split-K partial sums and per-column-block tickets)
+// is the fixed array below, compiled into the library: it allocates nothing.
+//
+// Limits and sharing rules:
+//   - the array holds kNoAllocScratchBytes = 4 MiB on every GPU that loads the
+//     library, until the process exits;
+//   - split-K partials need splitk * M * N * 4 bytes of the
+//     kNoAllocPartialBytes part, and the kernel needs ceil(N / 64) tickets of
+//     the kNoAllocTickets available; larger calls are rejected with
+//     VKBLAS_ERR_PARAM before anything is enqueued;
+//   - every call on a device shares the one array and it keeps the last
+//     call's contents, so each call first clears the tickets it will use on
+//     its stream; two calls whose kernels overlap on the GPU (different
+//     streams, no ordering between them) race on the array and give wrong
+//     results -- order such calls on one stream or with events;
+//   - the first call on each device looks up the array's device address with
+//     cudaGetSymbolAddress (with that device current); make that first call
+//     before any stream capture.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+constexpr size_t kNoAllocTickets = 4096;
+constexpr size_t kNoAllocTicketBytes = kNoAllocTickets * sizeof(unsigned);
+constexpr size_t kNoAllocPartialBytes = kNoAllocScratchBytes - kNoAllocTicketBytes;
+
+static __device__ __align__(256) unsigned char g_gemv_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace vkb {
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// The split-K GEMV launch with caller-placed tickets and partials.
+cudaError_t launch_gemv_layout(const GemmProblem& p, int splitk, void* tickets, void* partials,
+                               cudaStream_t s) {
+    uint32_t kspan = gemv_kspan(p.K, splitk);
+    uint32_t segs = (p.K + kspan - 1) / kspan;
+    if (segs < 1) segs = 1;
+    GemvArgs a;
+    a.X = p.A; a.ldx = p.lda; a.W = p.B; a.ldw = p.ldb; a.C = p.C; a.ldc = p.ldc;
+    a.M = p.M; a.N = p.N; a.K = p.K; a.kspan = kspan; a.splitk = segs;
+    a.alpha = p.alpha; a.beta = p.beta; a.d_alpha = p.d_alpha; a.d_beta = p.d_beta;
+    a.partial = segs > 1 ? reinterpret_cast<float*>(partials) : nullptr;
+    a.tickets = segs > 1 ? reinterpret_cast<unsigned*>(tickets) : nullptr;
+    dim3 grid((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA, segs);
+    const bool two = p.M > 8;
+    if (p.dtype == DT_F16) {
+        if (two) gemv_kernel<__half, true><<<grid, WARPS * 32, 0, s>>>(a);
+        else gemv_kernel<__half, false><<<grid, WARPS * 32, 0, s>>>(a);
+    } else {
+        if (two) gemv_kernel<__nv_bfloat16, true><<<grid, WARPS * 32, 0, s>>>(a);
+        else gemv_kernel<__nv_bfloat16, false><<<grid, WARPS * 32, 0, s>>>(a);
+    }
+    count_launch();
+    return cudaGetLastError();
+}
+
+// Device address of the scratch array on `dev` (the current device), looked up
+// once per device.  The host-side symbol itself is only a stand-in: passing it
+// to a kernel would fault or silently address host memory.
+void* noalloc_scratch(int dev) {
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_gemv_noalloc_scratch) != cudaSuccess || !ptr) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        g_noalloc_ptr[dev] = ptr;
+    }
+    return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+}  // namespace vkb
+
+extern "C" __attribute__((visibility("default"))) vkblas_status_t vkblas_gemv_splitk_noalloc(
+    vkblas_dtype_t dtype, uint32_t M, uint32_t N, uint32_t K, float alpha, const void* X,
+    uint32_t ldx, const void* W, uint32_t ldw, float beta, void* C, uint32_t ldc,
+    uint32_t splitk, void* stream) {
+    using namespace vkb;
+    if (dtype != VKBLAS_DT_F16 && dtype != VKBLAS_DT_BF16) return VKBLAS_ERR_PARAM;
+    if (M == 0 || N == 0 || K == 0 || !X || !W || !C || splitk < 1 || splitk > 16)
+        return VKBLAS_ERR_PARAM;
+    GemmProblem p;
+    p.dtype = dtype == VKBLAS_DT_F16 ? DT_F16 : DT_BF16;
+    p.op_a = 0;
+    p.op_b = 1;
+    p.M = M; p.N = N; p.K = K;
+    p.alpha = alpha; p.beta = beta;
+    p.d_alpha = nullptr; p.d_beta = nullptr;
+    p.A = X; p.lda = ldx; p.B = W; p.ldb = ldw; p.C = C; p.ldc = ldc;
+    p.batch = 1; p.sa = 0; p.sb = 0; p.sc = 0;
+    if (!gemv_supported(p)) return VKBLAS_ERR_PARAM;            // M <= 16, 16-byte alignment
+    const size_t ctas = (N + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+    if ((size_t)splitk * M * N * sizeof(float) > kNoAllocPartialBytes || ctas > kNoAllocTickets)
+        return VKBLAS_ERR_PARAM;                                 // beyond the fixed scratch
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        major != 10) {
+        cudaGetLastError();
+        return VKBLAS_ERR_INIT;
+    }
+    unsigned char* scratch = static_cast<unsigned char*>(noalloc_scratch(dev));
+    if (!scratch) return VKBLAS_ERR_INIT;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // The kernel expects zero tickets (it leaves them zero), and the array keeps
+    // whatever the last call left: clear the ones this call uses.
+    if (splitk > 1 && cudaMemsetAsync(scratch, 0, ctas * sizeof(unsigned), s) != cudaSuccess) {
+        cudaGetLastError();
+        return VKBLAS_ERR_INIT;
+    }
+    // Array layout: [tickets: kNoAllocTicketBytes][partials: kNoAllocPartialBytes].
+    cudaError_t e = launch_gemv_layout(p, (int)splitk, scratch, scratch + kNoAllocTicketBytes, s);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return e == cudaErrorInvalidValue ? VKBLAS_ERR_PARAM : VKBLAS_ERR_INIT;
+    }
+    return VKBLAS_OK;
+}
