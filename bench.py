@@ -162,10 +162,10 @@ def _time_loop(fn, iters, stream):
 def secondary_results(vk, hb, torch, peaks):
     """Other BASELINE configs on one GPU (device-resident inputs, CUDA events)."""
     out = {}
-    s = torch.cuda.current_stream()
+    s = torch.cuda.Stream()         # CUDA graphs cannot be captured on the default stream
     al, be = hb.fptr(1.0), hb.fptr(0.0)
     g = torch.Generator(device="cuda").manual_seed(3)
-    with hb.Handle() as h:
+    with hb.Handle() as h, torch.cuda.stream(s):
         h.set_stream(s)
         # config 3: HGEMM T/N 4096^3 and 8192^3
         for n in (4096, 8192):
@@ -187,7 +187,9 @@ def secondary_results(vk, hb, torch, peaks):
                                     "path": vk.PATH_NAMES[vk.last_path()],
                                     "frac_of_bf16_burst": round(tf / peaks["bf16_tflops"], 4)}
             del sets
-        # config 4: decode GEMV, 4 rotating weight sets (470 MB > L2)
+        # config 4: decode GEMV, 4 rotating weight sets (470 MB > L2).  Timed two
+        # ways: back-to-back calls (includes each call's launch gap) and a CUDA
+        # graph of 40 calls replayed (kernel time; what a decode loop captures).
         K, O = 4096, 14336
         Ws = [(torch.randn(O, K, device="cuda", generator=g) * 0.02).half() for _ in range(4)]
         for M in (1, 4, 16):
@@ -202,11 +204,20 @@ def secondary_results(vk, hb, torch, peaks):
             for i in range(4):
                 run(i)
             ms = _time_loop(run, 40, s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(40):
+                    run(i)
+            graph.replay()
+            ms_g = _time_loop(lambda i: graph.replay(), 5, s) / 40
+            del graph
             nbytes = 2.0 * (O * K + M * K + M * O)
-            gbs = nbytes / ms / 1e6
+            gbs, gbs_g = nbytes / ms / 1e6, nbytes / ms_g / 1e6
             out[f"gemv_m{M}"] = {"gbs": round(gbs, 1), "us": round(ms * 1e3, 2),
+                                 "gbs_graph": round(gbs_g, 1), "us_graph": round(ms_g * 1e3, 2),
                                  "path": vk.PATH_NAMES[vk.last_path()],
-                                 "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4)}
+                                 "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                                 "frac_of_hbm_graph": round(gbs_g / peaks["hbm_gbs"], 4)}
         del Ws
         # config 5: strided-batched 256 x 2048^3 NN
         b, n = 256, 2048

@@ -45,7 +45,7 @@ vkblas_status_t vkblas_gemm_ex(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op
  * batch 1, on `stream` (a cudaStream_t; NULL = legacy default stream), with
  * the K range split into `splitk` (1..16) segments.  Scratch is a fixed 4 MiB
  * array inside the library (held by every GPU that loads it until exit):
- * splitk*M*N*4 must fit in 4 MiB - 16 KiB and N in 4096*64 rows, and
+ * splitk*M*N*4 must fit in 4 MiB - 64 KiB and N in 16384*16 rows, and
  * M <= 16, K, ldx, ldw multiples of 8, X and W 16-byte aligned; otherwise
  * VKBLAS_ERR_PARAM and nothing is enqueued.  All calls on a device share the
  * array: calls whose kernels overlap on the GPU race (order them on one

@@ -1,0 +1,101 @@
+"""Run one GEMM case of the BASELINE configs a few times (for timing and ncu).
+
+    python -m vkblas_b200.cases sgemm  [--n 4096] [--iters 3]       # 3xTF32, hipBLAS N/N
+    python -m vkblas_b200.cases sgemm-simt [--n 4096]                # exact FFMA kernel
+    python -m vkblas_b200.cases hgemm  [--n 4096]                    # fp16 tcgen05, hipBLAS T/N
+    python -m vkblas_b200.cases gemv   [--m 1] [--splitk 4]          # decode GEMV, K=4096, N=14336
+    python -m vkblas_b200.cases batched                              # 256 x 2048^3 fp16 N/N
+
+Inputs are device-resident and seeded; each iteration is one library call on
+torch's current stream; the mean time per call (CUDA events) is printed.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+import vkblas_b200 as vk
+from vkblas_b200 import hipblas as hb
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["sgemm", "sgemm-simt", "hgemm", "gemv", "batched"])
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--splitk", type=int, default=0)
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args(argv)
+
+    torch.cuda.init()
+    s = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    h = hb.Handle()
+    h.set_stream(s)
+    n = a.n
+    if a.case in ("sgemm", "sgemm-simt"):
+        A = torch.randn(n * n, device="cuda", generator=g)
+        B = torch.randn(n * n, device="cuda", generator=g)
+        C = torch.empty(n * n, device="cuda")
+        if a.case == "sgemm-simt":
+            vk.set_path(vk.PATH_SIMT)
+        flop, nbytes = 2.0 * n ** 3, 0.0
+        call = lambda: vk.lib.hipblasSgemm(h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, n, n, n, al,  # noqa: E731
+                                           A.data_ptr(), n, B.data_ptr(), n, be, C.data_ptr(), n)
+    elif a.case == "hgemm":
+        A = (torch.randn(n * n, device="cuda", generator=g) * 0.02).half()
+        B = (torch.randn(n * n, device="cuda", generator=g) * 0.02).half()
+        C = torch.empty(n * n, device="cuda", dtype=torch.float16)
+        flop, nbytes = 2.0 * n ** 3, 0.0
+        call = lambda: vk.lib.hipblasGemmEx_v2(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, n, n, n, al,  # noqa: E731
+                                               A.data_ptr(), vk.HIP_R_16F, n, B.data_ptr(),
+                                               vk.HIP_R_16F, n, be, C.data_ptr(), vk.HIP_R_16F, n,
+                                               vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+    elif a.case == "gemv":
+        K, O, M = 4096, 14336, a.m
+        W = (torch.randn(O * K, device="cuda", generator=g) * 0.02).half()
+        X = torch.randn(M * K, device="cuda", generator=g).half()
+        C = torch.empty(M * O, device="cuda", dtype=torch.float16)
+        if a.splitk:
+            vk.set_splitk(a.splitk)
+        flop, nbytes = 2.0 * M * O * K, 2.0 * (O * K + M * K + M * O)
+        call = lambda: vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,  # noqa: E731
+                                            W.data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
+                                            vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F,
+                                            O, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+    else:
+        b, n = 256, 2048
+        A = (torch.randn(b * n * n, device="cuda", generator=g) * 0.02).half()
+        B = (torch.randn(b * n * n, device="cuda", generator=g) * 0.02).half()
+        C = torch.empty(b * n * n, device="cuda", dtype=torch.float16)
+        flop, nbytes = b * 2.0 * n ** 3, 0.0
+        call = lambda: vk.lib.hipblasGemmStridedBatchedEx_v2(  # noqa: E731
+            h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, n, n, n, al, A.data_ptr(), vk.HIP_R_16F, n,
+            n * n, B.data_ptr(), vk.HIP_R_16F, n, n * n, be, C.data_ptr(), vk.HIP_R_16F, n, n * n,
+            b, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+
+    st = call()
+    if st != 0:
+        raise SystemExit(f"status {st}")
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(a.iters):
+        call()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(1, a.iters)
+    st = vk.device_status(True)
+    line = f"{a.case}: {ms * 1e3:.2f} us/call, {flop / ms / 1e9:.2f} TFLOP/s"
+    if nbytes:
+        line += f", {nbytes / ms / 1e6:.1f} GB/s"
+    print(line + f", path={vk.PATH_NAMES[vk.last_path()]}, status={st}")
+    h.close()
+    return 0 if st == 0 else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <cuda.h>
 
 namespace vkb {
 
@@ -74,13 +75,19 @@ cudaError_t launch_simt_gemm(const GemmProblem& p, cudaStream_t s);
 bool gemv_supported(const GemmProblem& p);
 int gemv_auto_splitk(const GemmProblem& p, int num_sms);
 size_t gemv_workspace_bytes(const GemmProblem& p, int splitk);
-cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaStream_t s);
+cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, int* d_status,
+                        cudaStream_t s);
 bool umma_supported(const GemmProblem& p);
 bool umma_profitable(const GemmProblem& p);
 size_t umma_workspace_bytes(const GemmProblem& p);
 // cudaErrorNotSupported: the operands cannot be described to TMA (nothing launched).
 cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* workspace,
                              cudaStream_t s);
+// 2-D TMA tensor map over a 2-byte matrix [outer][inner] (row stride ld
+// elements), box [box_outer][box_inner], no swizzle.  False if the driver
+// entry point is missing or the layout cannot be described.
+bool encode_tmap_2d(CUtensorMap* m, bool bf16, const void* base, uint64_t inner, uint64_t outer,
+                    uint64_t ld, uint32_t box_inner, uint32_t box_outer);
 // Host-side launch counter (all kernels of this library).
 void count_launch();
 }  // namespace vkb

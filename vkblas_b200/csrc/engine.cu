@@ -188,7 +188,15 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
             ws = workspace(ds, 0, s, need);
             if (!ws) splitk = 1;
         }
-        e = launch_gemv(p, splitk, ws, s);
+        e = launch_gemv(p, splitk, ws, ds->d_status, s);
+        if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
+            cudaGetLastError();
+            path = VKBLAS_PATH_SIMT;       // weights TMA cannot describe: exact SIMT path
+            e = launch_simt_gemm(p, s);
+        } else if (e == cudaErrorNotSupported) {
+            cudaGetLastError();
+            return VKBLAS_ERR_FALLBACK;
+        }
     } else if (path == VKBLAS_PATH_TC) {
         const size_t need = umma_workspace_bytes(p);
         void* ws = need ? workspace(ds, 1, s, need) : nullptr;

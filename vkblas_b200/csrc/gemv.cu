@@ -6,20 +6,27 @@
 // sum_k X[m, k] * W[n, k] + beta * C[m, n] for M <= 16, with W stored as
 // N rows of K contiguous elements (the engine's op_b == T, i.e. hipBLAS
 // transA == T on the weights -- test/bench_decode.c:52-64).  fp32 accumulate,
-// fp32 epilogue, RNE store; with split-K the K range is cut into S segments
-// whose fp32 partials are summed in segment order before the epilogue
-// (splitk_reduce_half.comp:16-35).
+// fp32 epilogue, RNE store; split-K partial sums are added in segment order
+// before the epilogue (splitk_reduce_half.comp:16-35).
 //
 // The kernel is HBM-bound on the weight stream (2*N*K bytes), so its design
-// is about bytes in flight: every lane issues 128-bit loads of W rows, four
-// per 64-wide K chunk, two chunks unrolled.  The multiply runs on the tensor
-// cores through mma.sync m16n8k16 (W rows are the MMA's M, tokens its N) so
-// that the M = 16 case is not limited by the FP32 pipe; since only the sum
-// over k matters, each lane feeds the MMA the 8 consecutive k it loaded
-// (A and B see the same k permutation), which keeps every load 128 bits wide
-// without shared memory.  Split-K partials go to a workspace; the last CTA of
-// each column block (atomic ticket, no waiting) reduces them in segment
-// order, applies alpha/beta and resets its ticket for the next launch.
+// is about bytes in flight and resident warps:
+//   - a CTA owns 16 weight rows; its KW warps split the K range between them
+//     (intra-CTA split-K) and add their partial sums through shared memory
+//     in warp order, so parallelism comes without global partials;
+//   - every lane issues 128-bit loads of its rows straight into registers
+//     (8 per 128-wide K step).  Shared-memory rings (cp.async, bulk copies,
+//     2-D TMA) were measured slower here: the ring's footprint cut residency
+//     to 8 warps per SM, too few to hide the per-warp load and MMA latency;
+//   - the multiply runs on the tensor cores through mma.sync m16n8k16 (W rows
+//     are the MMA's M, tokens its N) so that M = 16 is not FP32-bound; since
+//     only the sum over k matters, each lane feeds the MMA the 8 consecutive k
+//     it loaded (A and B see the same k permutation);
+//   - optional inter-CTA split-K (gridDim.y segments) for short N: segment
+//     partials go to a workspace and the last CTA of each row block (atomic
+//     ticket, no waiting) reduces them in segment order, applies alpha/beta
+//     and resets its ticket for the next launch.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -28,8 +35,8 @@
 namespace vkb {
 namespace {
 
-constexpr int WARPS = 4;                 // 64 weight rows per CTA
-constexpr int ROWS_PER_CTA = WARPS * 16;
+constexpr int KW = 8;                    // warps per CTA, splitting K
+constexpr int ROWS_PER_CTA = 16;         // weight rows per CTA (one m16 MMA tile)
 constexpr int KCHUNK = 64;
 
 struct GemvArgs {
@@ -38,7 +45,7 @@ struct GemvArgs {
     void* C; uint32_t ldc;                // M x N output
     uint32_t M, N, K;
     uint32_t kspan;                       // K elements per segment (multiple of KCHUNK)
-    uint32_t splitk;
+    uint32_t splitk;                      // segments (gridDim.y)
     float alpha, beta;
     const float* d_alpha;
     const float* d_beta;
@@ -50,8 +57,7 @@ template <typename T> struct Mma;
 template <> struct Mma<__half> {
     static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4],
                                                uint32_t b0, uint32_t b1) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
             "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -60,24 +66,26 @@ template <> struct Mma<__half> {
 template <> struct Mma<__nv_bfloat16> {
     static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4],
                                                uint32_t b0, uint32_t b1) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
             "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
     }
 };
 
+// Weights: read once -> bypass L1, 256-byte L2 fetches (a step reads 256
+// contiguous bytes of each row).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
+// Activations: tiny and reused by every warp -> through L1.
 __device__ __forceinline__ uint4 ldg_cached(const void* p) {
     uint4 v;
-    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
 
@@ -93,13 +101,17 @@ __device__ __forceinline__ void mma_32k(float (&d)[4], const uint4& w_lo, const 
 }
 
 template <typename T, bool TWO_NTILES>
-__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(KW * 32) gemv_kernel(GemvArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t nbase = blockIdx.x * ROWS_PER_CTA + warp * 16;
+    const uint32_t nbase = blockIdx.x * ROWS_PER_CTA;
     const uint32_t seg = blockIdx.y;
     const uint32_t kbeg = seg * a.kspan;
     const uint32_t kend = min(a.K, kbeg + a.kspan);
+    // This warp's slice of the segment (multiples of KCHUNK).
+    const uint32_t per = ((kend - kbeg + KW - 1) / KW + KCHUNK - 1) / KCHUNK * KCHUNK;
+    const uint32_t kw0 = min(kend, kbeg + (uint32_t)warp * per);
+    const uint32_t kw1 = min(kend, kw0 + per);
 
     const T* W = reinterpret_cast<const T*>(a.W);
     const T* X = reinterpret_cast<const T*>(a.X);
@@ -115,9 +127,9 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
     float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 
-    uint32_t kb = kbeg;
-    // Two 64-wide chunks per iteration: 8 x 128-bit weight loads in flight per lane.
-    for (; kb + 2 * KCHUNK <= kend; kb += 2 * KCHUNK) {
+    uint32_t kb = kw0;
+    // Two 64-wide chunks per step: 8 x 128-bit weight loads in flight per lane.
+    for (; kb + 2 * KCHUNK <= kw1; kb += 2 * KCHUNK) {
         uint4 w[2][2][2];                   // [chunk][half][row]
 #pragma unroll
         for (int c = 0; c < 2; c++)
@@ -141,10 +153,10 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
             }
     }
     // Tail: 32-wide halves; K is a multiple of 8, so each lane's 8-wide block
-    // is entirely inside or entirely outside [kb, kend).
-    for (; kb < kend; kb += 32) {
+    // is entirely inside or entirely outside [kb, kw1).
+    for (; kb < kw1; kb += 32) {
         const uint32_t k = kb + 8 * t;
-        const bool in = k < kend;
+        const bool in = k < kw1;
         uint4 wl = (in && r0ok) ? ldg_stream(w0p + k) : z;
         uint4 wh = (in && r1ok) ? ldg_stream(w1p + k) : z;
         uint4 xa = (in && x0ok) ? ldg_cached(x0p + k) : z;
@@ -155,6 +167,28 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
         }
     }
 
+    // Warp partials -> shared memory; warp 0 adds them in warp (= k) order.
+    __shared__ float red[KW][TWO_NTILES ? 8 : 4][32];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        red[warp][i][lane] = d0[i];
+        if (TWO_NTILES) red[warp][4 + i][lane] = d1[i];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float s0 = red[0][i][lane], s1 = TWO_NTILES ? red[0][4 + i][lane] : 0.f;
+#pragma unroll
+            for (int w = 1; w < KW; w++) {
+                s0 = __fadd_rn(s0, red[w][i][lane]);
+                if (TWO_NTILES) s1 = __fadd_rn(s1, red[w][4 + i][lane]);
+            }
+            d0[i] = s0;
+            d1[i] = s1;
+        }
+    }
+
     float alpha = a.alpha, beta = a.beta;
     load_scalars(a.d_alpha, a.d_beta, alpha, beta);
     T* C = reinterpret_cast<T*>(a.C);
@@ -162,6 +196,7 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
     // Fragment ownership: d[0]=(n=r0, m=2t) d[1]=(r0, 2t+1) d[2]=(r1, 2t) d[3]=(r1, 2t+1);
     // n-tile 1 adds 8 to m.
     if (a.splitk == 1) {
+        if (warp != 0) return;
 #pragma unroll
         for (int nt = 0; nt < (TWO_NTILES ? 2 : 1); nt++) {
             const float* d = nt ? d1 : d0;
@@ -179,19 +214,21 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
         return;
     }
 
-    // Split-K: publish this segment's partials, then take a ticket.
-    float* P = a.partial + (size_t)seg * a.M * a.N;
+    // Inter-CTA split-K: publish this segment's partials, then take a ticket.
+    if (warp == 0) {
+        float* P = a.partial + (size_t)seg * a.M * a.N;
 #pragma unroll
-    for (int nt = 0; nt < (TWO_NTILES ? 2 : 1); nt++) {
-        const float* d = nt ? d1 : d0;
+        for (int nt = 0; nt < (TWO_NTILES ? 2 : 1); nt++) {
+            const float* d = nt ? d1 : d0;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t n = (i < 2) ? r0 : r1;
-            const uint32_t m = nt * 8 + 2 * t + (i & 1);
-            if (n < a.N && m < a.M) __stcg(P + (size_t)m * a.N + n, d[i]);
+            for (int i = 0; i < 4; i++) {
+                const uint32_t n = (i < 2) ? r0 : r1;
+                const uint32_t m = nt * 8 + 2 * t + (i & 1);
+                if (n < a.N && m < a.M) __stcg(P + (size_t)m * a.N + n, d[i]);
+            }
         }
+        __threadfence();
     }
-    __threadfence();
     __syncthreads();
     __shared__ unsigned s_last;
     if (threadIdx.x == 0) {
@@ -201,11 +238,10 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // Last CTA of this column block: sum the partials in segment order.
-    const uint32_t ncta0 = blockIdx.x * ROWS_PER_CTA;
+    // Last CTA of this row block: sum the partials in segment order.
     const uint32_t cells = (uint32_t)ROWS_PER_CTA * a.M;
-    for (uint32_t e = threadIdx.x; e < cells; e += WARPS * 32) {
-        const uint32_t m = e / ROWS_PER_CTA, n = ncta0 + e % ROWS_PER_CTA;
+    for (uint32_t e = threadIdx.x; e < cells; e += KW * 32) {
+        const uint32_t m = e / ROWS_PER_CTA, n = nbase + e % ROWS_PER_CTA;
         if (n >= a.N) continue;
         float s = 0.f;
         for (uint32_t q = 0; q < a.splitk; q++)
@@ -219,6 +255,41 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+uint32_t gemv_kspan(uint32_t K, int splitk) {
+    uint32_t span = (K + splitk - 1) / splitk;
+    return (span + KCHUNK - 1) / KCHUNK * KCHUNK;
+}
+
+// One launch over segments [0, segs) with the given partial/ticket areas
+// (both unused when a single segment results).
+cudaError_t launch_segments(const GemmProblem& p, int splitk, float* partial, unsigned* tickets,
+                            cudaStream_t s) {
+    if (splitk < 1) splitk = 1;
+    uint32_t kspan = gemv_kspan(p.K, splitk);
+    uint32_t segs = (p.K + kspan - 1) / kspan;        // may be < splitk after rounding
+    if (segs < 1) segs = 1;
+    if (segs > 1 && (!partial || !tickets)) return cudaErrorInvalidValue;
+    GemvArgs a;
+    a.X = p.A; a.ldx = p.lda; a.W = p.B; a.ldw = p.ldb; a.C = p.C; a.ldc = p.ldc;
+    a.M = p.M; a.N = p.N; a.K = p.K; a.kspan = kspan; a.splitk = segs;
+    a.alpha = p.alpha; a.beta = p.beta; a.d_alpha = p.d_alpha; a.d_beta = p.d_beta;
+    a.partial = segs > 1 ? partial : nullptr;
+    a.tickets = segs > 1 ? tickets : nullptr;
+    dim3 grid((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA, segs);
+    const bool two = p.M > 8;
+    if (p.dtype == DT_F16) {
+        if (two) gemv_kernel<__half, true><<<grid, KW * 32, 0, s>>>(a);
+        else gemv_kernel<__half, false><<<grid, KW * 32, 0, s>>>(a);
+    } else if (p.dtype == DT_BF16) {
+        if (two) gemv_kernel<__nv_bfloat16, true><<<grid, KW * 32, 0, s>>>(a);
+        else gemv_kernel<__nv_bfloat16, false><<<grid, KW * 32, 0, s>>>(a);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    count_launch();
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 bool gemv_supported(const GemmProblem& p) {
@@ -228,16 +299,13 @@ bool gemv_supported(const GemmProblem& p) {
 }
 
 int gemv_auto_splitk(const GemmProblem& p, int num_sms) {
+    // The KW warps of a CTA already split K; cut K across CTAs too only when
+    // there are too few row blocks to keep every SM busy.
     const uint32_t ctas = (p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
     int s = 1;
-    // Aim for >= 4 CTAs (16 warps) per SM while keeping >= 512 K per segment.
-    while (s < 16 && ctas * s < 4u * (uint32_t)num_sms && p.K / (2u * s) >= 512u) s *= 2;
+    while (s < 16 && ctas * s < 3u * (uint32_t)num_sms && p.K / (2u * s) >= (uint32_t)KW * 128u)
+        s *= 2;
     return s;
-}
-
-static uint32_t gemv_kspan(uint32_t K, int splitk) {
-    uint32_t span = (K + splitk - 1) / splitk;
-    return (span + KCHUNK - 1) / KCHUNK * KCHUNK;
 }
 
 // Workspace layout: [tickets: MAX_TICKETS x u32, zero on entry and left zero
@@ -252,36 +320,16 @@ size_t gemv_workspace_bytes(const GemmProblem& p, int splitk) {
     return TICKET_BYTES + (size_t)splitk * p.M * p.N * sizeof(float);
 }
 
-cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaStream_t s) {
-    if (splitk < 1) splitk = 1;
-    uint32_t kspan = gemv_kspan(p.K, splitk);
-    uint32_t segs = (p.K + kspan - 1) / kspan;        // may be < splitk after rounding
-    if (segs < 1) segs = 1;
+cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, int* d_status,
+                        cudaStream_t s) {
+    (void)d_status;     // this kernel never waits on another CTA
     const uint32_t ctas = (p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
-    if (segs > 1 && ctas > MAX_TICKETS) return cudaErrorInvalidValue;
-    GemvArgs a;
-    a.X = p.A; a.ldx = p.lda; a.W = p.B; a.ldw = p.ldb; a.C = p.C; a.ldc = p.ldc;
-    a.M = p.M; a.N = p.N; a.K = p.K; a.kspan = kspan; a.splitk = segs;
-    a.alpha = p.alpha; a.beta = p.beta; a.d_alpha = p.d_alpha; a.d_beta = p.d_beta;
-    a.partial = nullptr; a.tickets = nullptr;
-    if (segs > 1) {
-        if (!workspace) return cudaErrorInvalidValue;
-        a.tickets = reinterpret_cast<unsigned*>(workspace);
-        a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + TICKET_BYTES);
-    }
-    dim3 grid((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA, segs);
-    const bool two = p.M > 8;
-    if (p.dtype == DT_F16) {
-        if (two) gemv_kernel<__half, true><<<grid, WARPS * 32, 0, s>>>(a);
-        else gemv_kernel<__half, false><<<grid, WARPS * 32, 0, s>>>(a);
-    } else if (p.dtype == DT_BF16) {
-        if (two) gemv_kernel<__nv_bfloat16, true><<<grid, WARPS * 32, 0, s>>>(a);
-        else gemv_kernel<__nv_bfloat16, false><<<grid, WARPS * 32, 0, s>>>(a);
-    } else {
-        return cudaErrorInvalidValue;
-    }
-    count_launch();
-    return cudaGetLastError();
+    if (splitk > 1 && (ctas > MAX_TICKETS || !workspace)) splitk = 1;
+    unsigned* tickets = reinterpret_cast<unsigned*>(workspace);
+    float* partial = workspace ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                                          TICKET_BYTES)
+                               : nullptr;
+    return launch_segments(p, splitk, partial, tickets, s);
 }
 
 }  // namespace vkb
@@ -295,15 +343,15 @@ cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaS
 // decode loops, where the grow-only workspace behind vkblas_gemm_f16 may free
 // and reallocate when a larger shape appears -- and cudaFree / cudaMalloc
 // synchronise the whole device.  This entry point runs the same split-K GEMV
-// kernel, but its scratch (split-K partial sums and per-column-block tickets)
+// kernel, but its scratch (split-K partial sums and per-row-block tickets)
 // is the fixed array below, compiled into the library: it allocates nothing.
 //
 // Limits and sharing rules:
 //   - the array holds kNoAllocScratchBytes = 4 MiB on every GPU that loads the
 //     library, until the process exits;
 //   - split-K partials need splitk * M * N * 4 bytes of the
-//     kNoAllocPartialBytes part, and the kernel needs ceil(N / 64) tickets of
-//     the kNoAllocTickets available; larger calls are rejected with
+//     kNoAllocPartialBytes part, and the kernel needs one ticket per 16 weight
+//     rows of the kNoAllocTickets available; larger calls are rejected with
 //     VKBLAS_ERR_PARAM before anything is enqueued;
 //   - every call on a device shares the one array and it keeps the last
 //     call's contents, so each call first clears the tickets it will use on
@@ -314,7 +362,7 @@ cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, cudaS
 //     cudaGetSymbolAddress (with that device current); make that first call
 //     before any stream capture.
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
-constexpr size_t kNoAllocTickets = 4096;
+constexpr size_t kNoAllocTickets = 16384;
 constexpr size_t kNoAllocTicketBytes = kNoAllocTickets * sizeof(unsigned);
 constexpr size_t kNoAllocPartialBytes = kNoAllocScratchBytes - kNoAllocTicketBytes;
 
@@ -325,31 +373,6 @@ namespace {
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {};
-
-// The split-K GEMV launch with caller-placed tickets and partials.
-cudaError_t launch_gemv_layout(const GemmProblem& p, int splitk, void* tickets, void* partials,
-                               cudaStream_t s) {
-    uint32_t kspan = gemv_kspan(p.K, splitk);
-    uint32_t segs = (p.K + kspan - 1) / kspan;
-    if (segs < 1) segs = 1;
-    GemvArgs a;
-    a.X = p.A; a.ldx = p.lda; a.W = p.B; a.ldw = p.ldb; a.C = p.C; a.ldc = p.ldc;
-    a.M = p.M; a.N = p.N; a.K = p.K; a.kspan = kspan; a.splitk = segs;
-    a.alpha = p.alpha; a.beta = p.beta; a.d_alpha = p.d_alpha; a.d_beta = p.d_beta;
-    a.partial = segs > 1 ? reinterpret_cast<float*>(partials) : nullptr;
-    a.tickets = segs > 1 ? reinterpret_cast<unsigned*>(tickets) : nullptr;
-    dim3 grid((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA, segs);
-    const bool two = p.M > 8;
-    if (p.dtype == DT_F16) {
-        if (two) gemv_kernel<__half, true><<<grid, WARPS * 32, 0, s>>>(a);
-        else gemv_kernel<__half, false><<<grid, WARPS * 32, 0, s>>>(a);
-    } else {
-        if (two) gemv_kernel<__nv_bfloat16, true><<<grid, WARPS * 32, 0, s>>>(a);
-        else gemv_kernel<__nv_bfloat16, false><<<grid, WARPS * 32, 0, s>>>(a);
-    }
-    count_launch();
-    return cudaGetLastError();
-}
 
 // Device address of the scratch array on `dev` (the current device), looked up
 // once per device.  The host-side symbol itself is only a stand-in: passing it
@@ -409,7 +432,9 @@ extern "C" __attribute__((visibility("default"))) vkblas_status_t vkblas_gemv_sp
         return VKBLAS_ERR_INIT;
     }
     // Array layout: [tickets: kNoAllocTicketBytes][partials: kNoAllocPartialBytes].
-    cudaError_t e = launch_gemv_layout(p, (int)splitk, scratch, scratch + kNoAllocTicketBytes, s);
+    cudaError_t e = launch_segments(p, (int)splitk,
+                                    reinterpret_cast<float*>(scratch + kNoAllocTicketBytes),
+                                    reinterpret_cast<unsigned*>(scratch), s);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return e == cudaErrorInvalidValue ? VKBLAS_ERR_PARAM : VKBLAS_ERR_INIT;

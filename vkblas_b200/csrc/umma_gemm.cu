@@ -590,6 +590,20 @@ constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
 
 }  // namespace
 
+bool encode_tmap_2d(CUtensorMap* m, bool bf16, const void* base, uint64_t inner, uint64_t outer,
+                    uint64_t ld, uint32_t box_inner, uint32_t box_outer) {
+    auto enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+               const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool umma_supported(const GemmProblem& p) {
     if (!encode_fn()) return false;
     if (p.dtype == DT_F16 || p.dtype == DT_BF16)
