@@ -75,6 +75,13 @@ void vkblas_b200_set_splitk(int splitk);
  * error).  Synchronises the current device first.  clear != 0 resets it. */
 int vkblas_b200_device_status(int clear);
 
+/* Test hook for the bounded waits (thread-local, off by default): while on,
+ * tcgen05 GEMMs launched from this thread leave their first shared-memory
+ * stage unfilled and wait at most 20 ms, so the MMA warp's wait runs out, the
+ * kernel records status 2 (MMA wait timeout) in the device status word and
+ * every role unwinds; the context stays usable.  For tests only. */
+void vkblas_b200_set_test_stall(int on);
+
 /* Number of kernels this library launched from the calling process (all
  * threads); used by tests and benchmarks to prove the native path ran. */
 uint64_t vkblas_b200_launch_count(void);

@@ -61,6 +61,7 @@ def _load() -> C.CDLL:
     lib.vkblas_b200_get_path.restype = i32
     lib.vkblas_b200_last_path.restype = i32
     lib.vkblas_b200_set_splitk.argtypes = [i32]
+    lib.vkblas_b200_set_test_stall.argtypes = [i32]
     lib.vkblas_b200_device_status.argtypes = [i32]
     lib.vkblas_b200_device_status.restype = i32
     lib.vkblas_b200_launch_count.restype = C.c_uint64
@@ -72,44 +73,58 @@ def _load() -> C.CDLL:
     return lib
 
 
-lib = _load()
+_lib = None
+
+
+def _get() -> C.CDLL:
+    """The loaded library (loaded on first use, so that building it does not need it)."""
+    global _lib
+    if _lib is None:
+        _lib = _load()
+    return _lib
+
+
+def __getattr__(name):
+    if name == "lib":
+        return _get()
+    raise AttributeError(name)
 
 
 def version() -> str:
-    return lib.vkblas_b200_version().decode()
+    return _get().vkblas_b200_version().decode()
 
 
 def set_stream(stream) -> None:
     """Stream (cudaStream_t as int, or a torch.cuda.Stream) for this thread's calls."""
     if stream is not None and hasattr(stream, "cuda_stream"):
         stream = stream.cuda_stream
-    lib.vkblas_set_stream(C.c_void_p(stream or 0))
+    _get().vkblas_set_stream(C.c_void_p(stream or 0))
 
 
 def set_path(path: int) -> None:
-    lib.vkblas_b200_set_path(int(path))
+    _get().vkblas_b200_set_path(int(path))
 
 
 def last_path() -> int:
-    return lib.vkblas_b200_last_path()
+    return _get().vkblas_b200_last_path()
 
 
 def set_splitk(s: int) -> None:
-    lib.vkblas_b200_set_splitk(int(s))
+    _get().vkblas_b200_set_splitk(int(s))
 
 
 def device_status(clear: bool = True) -> int:
-    return lib.vkblas_b200_device_status(1 if clear else 0)
+    return _get().vkblas_b200_device_status(1 if clear else 0)
 
 
 def launch_count() -> int:
-    return int(lib.vkblas_b200_launch_count())
+    return int(_get().vkblas_b200_launch_count())
 
 
 def shard_range(units: int, rank: int, world: int, block: int = 1):
     b = C.c_uint64()
     n = C.c_uint64()
-    st = lib.vkblas_shard_range(units, block, rank, world, C.byref(b), C.byref(n))
+    st = _get().vkblas_shard_range(units, block, rank, world, C.byref(b), C.byref(n))
     if st != VKBLAS_OK:
         raise VkblasError(f"vkblas_shard_range status {st}")
     return int(b.value), int(n.value)
@@ -124,7 +139,7 @@ def gemm(dtype: int, op_a: int, op_b: int, M: int, N: int, K: int, alpha: float,
     """Row-major engine call (reference src/vkblas.h:19-36) on raw device pointers.
 
     Returns the vkblas_status_t value."""
-    fn = getattr(lib, _GEMM_BY_DTYPE[dtype])
+    fn = getattr(_get(), _GEMM_BY_DTYPE[dtype])
     return fn(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C_, ldc, batch, sa, sb, sc)
 
 

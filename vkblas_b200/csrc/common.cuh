@@ -81,8 +81,10 @@ bool umma_supported(const GemmProblem& p);
 bool umma_profitable(const GemmProblem& p);
 size_t umma_workspace_bytes(const GemmProblem& p);
 // cudaErrorNotSupported: the operands cannot be described to TMA (nothing launched).
+// test_stall: test hook, the producer leaves the first stage empty so the
+// MMA warp's bounded wait runs out (status DS_TIMEOUT_MMA) after 20 ms.
 cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* workspace,
-                             cudaStream_t s);
+                             bool test_stall, cudaStream_t s);
 // 2-D TMA tensor map over a 2-byte matrix [outer][inner] (row stride ld
 // elements), box [box_outer][box_inner], no swizzle.  False if the driver
 // entry point is missing or the layout cannot be described.

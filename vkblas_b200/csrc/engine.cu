@@ -132,6 +132,7 @@ struct ThreadState {
     int path = VKBLAS_PATH_AUTO;
     int splitk = 0;
     int last = VKBLAS_PATH_AUTO;
+    int test_stall = 0;
 };
 thread_local ThreadState tls;
 
@@ -200,7 +201,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     } else if (path == VKBLAS_PATH_TC) {
         const size_t need = umma_workspace_bytes(p);
         void* ws = need ? workspace(ds, 1, s, need) : nullptr;
-        e = (need && !ws) ? cudaErrorNotSupported : launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, s);
+        e = (need && !ws) ? cudaErrorNotSupported : launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, tls.test_stall != 0, s);
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
             cudaGetLastError();
             path = VKBLAS_PATH_SIMT;       // operands TMA cannot describe: exact SIMT path
@@ -343,6 +344,8 @@ VKB_EXPORT int vkblas_b200_last_path(void) { return tls.last; }
 VKB_EXPORT void vkblas_b200_set_splitk(int splitk) {
     tls.splitk = splitk < 0 ? 0 : splitk > 16 ? 16 : splitk;
 }
+
+VKB_EXPORT void vkblas_b200_set_test_stall(int on) { tls.test_stall = on ? 1 : 0; }
 
 VKB_EXPORT int vkblas_b200_device_status(int clear) {
     int dev = 0;

@@ -49,7 +49,8 @@ enum Kind : int { K_F16 = 0, K_BF16 = 1, K_TF32X3 = 2 };
 
 constexpr int BM = 128;
 constexpr uint32_t ROW_BYTES = 128;       // one SWIZZLE_128B atom row
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;       // 2 s
+constexpr uint64_t TEST_WAIT_LIMIT_NS = 20000000ull;    // 20 ms when the test hook is on
 constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;
 
 struct __align__(64) UmmaParams {
@@ -66,6 +67,8 @@ struct __align__(64) UmmaParams {
     const float* d_beta;
     int* status;
     uint32_t c_vec_ok;
+    uint64_t wait_limit_ns;      // bound of every mbarrier wait
+    uint32_t test_skip_first_load;   // test hook: the first stage is never filled
 };
 
 template <int KIND> struct OutT;
@@ -239,11 +242,20 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                 const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
                 for (uint32_t kb = 0; kb < p.num_kb; kb++) {
                     if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
-                                  DS_TIMEOUT_PRODUCER, WAIT_LIMIT_NS)) {
+                                  DS_TIMEOUT_PRODUCER, p.wait_limit_ns)) {
                         ok = false;
                         break;
                     }
                     const uint32_t fb = full_bar(stage);
+                    if (p.test_skip_first_load && t == blockIdx.x && kb == 0) {
+                        // Test hook: leave this stage empty so its consumer's
+                        // bounded wait runs out (no copy is issued).
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                        continue;
+                    }
                     mbar_arrive_expect_tx(fb, C_::STAGE_BYTES);
                     const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
                     const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
@@ -290,7 +302,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                 for (uint32_t sg = 0; ok && sg < nseg; sg++, u++) {
                     const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
                     if (!wait_bar(tempty_bar(buf), bph ^ 1u, abort_flag, p.status, DS_TIMEOUT_MMA,
-                                  WAIT_LIMIT_NS)) {
+                                  p.wait_limit_ns)) {
                         ok = false;
                         break;
                     }
@@ -300,7 +312,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                     const uint32_t kb1 = min(p.num_kb, kb0 + seg_kb);
                     for (uint32_t kb = kb0; kb < kb1; kb++) {
                         if (!wait_bar(full_bar(stage), phase, abort_flag, p.status, DS_TIMEOUT_MMA,
-                                      WAIT_LIMIT_NS)) {
+                                      p.wait_limit_ns)) {
                             ok = false;
                             break;
                         }
@@ -361,7 +373,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
             if constexpr (C_::SEG_KB == 0) {
                 const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
                 ok = wait_bar(tfull_bar(buf), bph, abort_flag, p.status, DS_TIMEOUT_EPILOGUE,
-                              WAIT_LIMIT_NS);
+                              p.wait_limit_ns);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc_fence_after();
@@ -383,7 +395,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                 for (uint32_t sg = 0; sg < nseg; sg++, u++) {
                     const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
                     ok = wait_bar(tfull_bar(buf), bph, abort_flag, p.status, DS_TIMEOUT_EPILOGUE,
-                                  WAIT_LIMIT_NS);
+                                  p.wait_limit_ns);
                     ok = __all_sync(0xffffffffu, ok);
                     if (!ok) break;
                     tc_fence_after();
@@ -628,9 +640,11 @@ size_t umma_workspace_bytes(const GemmProblem& p) {
 }
 
 cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* ws,
-                             cudaStream_t s) {
+                             bool test_stall, cudaStream_t s) {
     UmmaParams prm;
     memset(&prm, 0, sizeof(prm));
+    prm.wait_limit_ns = test_stall ? TEST_WAIT_LIMIT_NS : WAIT_LIMIT_NS;
+    prm.test_skip_first_load = test_stall ? 1u : 0u;
     const Operand a = operand_a(p), b = operand_b(p);
     const bool is32 = p.dtype == DT_F32;
     const int BN = is32 ? BN_TF32 : BN_16;
