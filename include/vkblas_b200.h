@@ -68,6 +68,10 @@ void vkblas_b200_set_path(int path);
 int vkblas_b200_get_path(void);
 /* Path taken by the last successful call on this thread (vkblas_path_t). */
 int vkblas_b200_last_path(void);
+/* K-split count of that call: the GEMV split-K factor, or for the tensor-core
+ * path the number of K ranges the tiles of its last, partial wave were cut
+ * into (their partial sums are added by a second kernel); 1 = no split. */
+int vkblas_b200_last_split(void);
 /* Thread-local split-K factor for the GEMV path: 0 = automatic, else 1..16. */
 void vkblas_b200_set_splitk(int splitk);
 

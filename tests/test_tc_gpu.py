@@ -32,7 +32,7 @@ def _mk(dtype, rng, n):
     return orc.widen(1 if dtype == vk.DT_BF16 else 0, bits), bits
 
 
-def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8):
+def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8, split=None):
     import torch
     rng = np.random.default_rng(M * 7 + N * 3 + K + op_a * 2 + op_b + dtype * 11 + batch)
     lda = (M if op_a else K)
@@ -70,6 +70,8 @@ def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8
         vk.set_path(vk.PATH_AUTO)
     assert st == vk.VKBLAS_OK, f"status {st}"
     assert vk.last_path() == vk.PATH_TC
+    if split is not None:
+        assert (vk.last_split() > 1) == split, f"K-split count {vk.last_split()}"
     check_status()
     got = host(dC) if dtype == vk.DT_F32 else orc.widen(dt16, host_u16(dC))
     want = orc.gemm_rowmajor_f64(op_a, op_b, M, N, K, alpha, np.ascontiguousarray(Af), lda,
@@ -90,6 +92,42 @@ def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8
 def test_tc_gemm(dtype, ops, shape, cuda):
     M, N, K = shape
     _run(dtype, ops[0], ops[1], M, N, K, 1.0, 0.0)
+
+
+# Fewer tiles than SMs: each tile's K range is cut into splits whose fp32
+# partials a second kernel adds in split order (split-K), when enough K work
+# per tile is saved.  (shape, splits for 2-byte types, splits for fp32)
+SPLIT_SHAPES = [
+    ((256, 256, 4096), True, True),
+    ((256, 384, 8192), True, True),
+    ((200, 300, 6000), True, True),      # ragged M, N and K
+    ((512, 512, 2048), False, True),     # too little K per tile to split fp16
+    ((384, 640, 1024), False, True),
+]
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_BF16, vk.DT_F32], ids=["f16", "bf16", "f32"])
+@pytest.mark.parametrize("ops", [(0, 0), (0, 1), (1, 0), (1, 1)], ids=["NN", "NT", "TN", "TT"])
+@pytest.mark.parametrize("case", SPLIT_SHAPES, ids=[f"{m}x{n}x{k}" for (m, n, k), _, _ in SPLIT_SHAPES])
+def test_tc_gemm_split_k(dtype, ops, case, cuda):
+    (M, N, K), split16, split32 = case
+    _run(dtype, ops[0], ops[1], M, N, K, 1.25, 0.5,
+         split=split32 if dtype == vk.DT_F32 else split16)
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_F32], ids=["f16", "f32"])
+def test_tc_split_k_batched_broadcast(dtype, cuda):
+    _run(dtype, 0, 1, 192, 200, 4096, 1.0, -1.0, batch=2, bcast="b", split=True)
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_F32], ids=["f16", "f32"])
+def test_tc_split_k_tail(dtype, cuda):
+    """More tiles than SMs (one tile per batch entry): whole waves run unsplit
+    and only the last, partial wave is split along K (stream-K tail)."""
+    if dtype == vk.DT_F32:
+        _run(dtype, 0, 0, 64, 72, 1536, 1.0, 0.25, batch=150, split=True)
+    else:
+        _run(dtype, 1, 1, 64, 72, 4096, 0.5, 0.0, batch=149, split=True)
 
 
 @pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_BF16, vk.DT_F32], ids=["f16", "bf16", "f32"])

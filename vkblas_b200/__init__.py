@@ -60,6 +60,7 @@ def _load() -> C.CDLL:
     lib.vkblas_b200_set_path.argtypes = [i32]
     lib.vkblas_b200_get_path.restype = i32
     lib.vkblas_b200_last_path.restype = i32
+    lib.vkblas_b200_last_split.restype = i32
     lib.vkblas_b200_set_splitk.argtypes = [i32]
     lib.vkblas_b200_set_test_stall.argtypes = [i32]
     lib.vkblas_b200_device_status.argtypes = [i32]
@@ -107,6 +108,11 @@ def set_path(path: int) -> None:
 
 def last_path() -> int:
     return _get().vkblas_b200_last_path()
+
+
+def last_split() -> int:
+    """K-split count of this thread's last call (1 = none)."""
+    return _get().vkblas_b200_last_split()
 
 
 def set_splitk(s: int) -> None:

@@ -1,8 +1,8 @@
 """Run one GEMM case of the BASELINE configs a few times (for timing and ncu).
 
-    python -m vkblas_b200.cases sgemm  [--n 4096] [--iters 3]       # 3xTF32, hipBLAS N/N
+    python -m vkblas_b200.cases sgemm  [--n 4096] [--shape M,N,K] [--iters 3]   # 3xTF32, N/N
     python -m vkblas_b200.cases sgemm-simt [--n 4096]                # exact FFMA kernel
-    python -m vkblas_b200.cases hgemm  [--n 4096]                    # fp16 tcgen05, hipBLAS T/N
+    python -m vkblas_b200.cases hgemm  [--n 4096] [--shape M,N,K]    # fp16 tcgen05, hipBLAS T/N
     python -m vkblas_b200.cases gemv   [--m 1] [--splitk 4]          # decode GEMV, K=4096, N=14336
     python -m vkblas_b200.cases batched                              # 256 x 2048^3 fp16 N/N
 
@@ -23,6 +23,7 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sgemm", "sgemm-simt", "hgemm", "gemv", "batched"])
     ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--shape", default="", help="M,N,K (sgemm, sgemm-simt, hgemm); default n,n,n")
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--splitk", type=int, default=0)
     ap.add_argument("--iters", type=int, default=3)
@@ -35,23 +36,26 @@ def main(argv=None) -> int:
     h = hb.Handle()
     h.set_stream(s)
     n = a.n
+    M, N, K = (int(x) for x in a.shape.split(",")) if a.shape else (n, n, n)
     if a.case in ("sgemm", "sgemm-simt"):
-        A = torch.randn(n * n, device="cuda", generator=g)
-        B = torch.randn(n * n, device="cuda", generator=g)
-        C = torch.empty(n * n, device="cuda")
+        A = torch.randn(M * K, device="cuda", generator=g)
+        B = torch.randn(K * N, device="cuda", generator=g)
+        C = torch.empty(M * N, device="cuda")
         if a.case == "sgemm-simt":
             vk.set_path(vk.PATH_SIMT)
-        flop, nbytes = 2.0 * n ** 3, 0.0
-        call = lambda: vk.lib.hipblasSgemm(h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, n, n, n, al,  # noqa: E731
-                                           A.data_ptr(), n, B.data_ptr(), n, be, C.data_ptr(), n)
+        flop, nbytes = 2.0 * M * N * K, 0.0
+        # column-major C (M x N) = A (M x K) * B (K x N)
+        call = lambda: vk.lib.hipblasSgemm(h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, M, N, K, al,  # noqa: E731
+                                           A.data_ptr(), M, B.data_ptr(), K, be, C.data_ptr(), M)
     elif a.case == "hgemm":
-        A = (torch.randn(n * n, device="cuda", generator=g) * 0.02).half()
-        B = (torch.randn(n * n, device="cuda", generator=g) * 0.02).half()
-        C = torch.empty(n * n, device="cuda", dtype=torch.float16)
-        flop, nbytes = 2.0 * n ** 3, 0.0
-        call = lambda: vk.lib.hipblasGemmEx_v2(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, n, n, n, al,  # noqa: E731
-                                               A.data_ptr(), vk.HIP_R_16F, n, B.data_ptr(),
-                                               vk.HIP_R_16F, n, be, C.data_ptr(), vk.HIP_R_16F, n,
+        A = (torch.randn(M * K, device="cuda", generator=g) * 0.02).half()
+        B = (torch.randn(K * N, device="cuda", generator=g) * 0.02).half()
+        C = torch.empty(M * N, device="cuda", dtype=torch.float16)
+        flop, nbytes = 2.0 * M * N * K, 0.0
+        # column-major C (M x N) = A^T (A stored K x M) * B (K x N)
+        call = lambda: vk.lib.hipblasGemmEx_v2(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, M, N, K, al,  # noqa: E731
+                                               A.data_ptr(), vk.HIP_R_16F, K, B.data_ptr(),
+                                               vk.HIP_R_16F, K, be, C.data_ptr(), vk.HIP_R_16F, M,
                                                vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
     elif a.case == "gemv":
         K, O, M = 4096, 14336, a.m

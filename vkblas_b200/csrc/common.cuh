@@ -80,11 +80,14 @@ cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, int* 
 bool umma_supported(const GemmProblem& p);
 bool umma_profitable(const GemmProblem& p);
 size_t umma_workspace_bytes(const GemmProblem& p);
+// Split-K / stream-K tail scratch: [tickets (zero, left zero)][partials]; 0 = no split.
+size_t umma_split_workspace_bytes(const GemmProblem& p, int num_sms);
+int umma_split_count(const GemmProblem& p, int num_sms);   // K splits of the last wave (1 = none)
 // cudaErrorNotSupported: the operands cannot be described to TMA (nothing launched).
 // test_stall: test hook, the producer leaves the first stage empty so the
 // MMA warp's bounded wait runs out (status DS_TIMEOUT_MMA) after 20 ms.
 cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* workspace,
-                             bool test_stall, cudaStream_t s);
+                             void* split_workspace, bool test_stall, cudaStream_t s);
 // 2-D TMA tensor map over a 2-byte matrix [outer][inner] (row stride ld
 // elements), box [box_outer][box_inner], no swizzle.  False if the driver
 // entry point is missing or the layout cannot be described.

@@ -17,6 +17,7 @@
 //      (simt_gemm.cu), which accepts every op, ld and stride.
 // Environment overrides, read once: VKBLAS_SGEMM=ffma|3xtf32|auto,
 // VKBLAS_HGEMM=simt|tc|auto, VKBLAS_GEMV=0|1, VKBLAS_GEMV_SPLITK=n,
+// VKBLAS_TC_SPLIT=0|1 (K-split of the tensor-core GEMM's last wave),
 // VKBLAS_TRACE=1 (one line per call on stderr).
 #include <atomic>
 #include <cstdio>
@@ -40,6 +41,7 @@ struct Config {
     int hgemm = 0;      // 0 auto, 1 simt, 2 tc
     int gemv = 1;
     int gemv_splitk = 0;
+    bool tc_split = true;
     bool trace = false;
 };
 
@@ -56,6 +58,7 @@ const Config& config() {
         }
         if (const char* e = getenv("VKBLAS_GEMV")) k.gemv = atoi(e) != 0;
         if (const char* e = getenv("VKBLAS_GEMV_SPLITK")) k.gemv_splitk = atoi(e);
+        if (const char* e = getenv("VKBLAS_TC_SPLIT")) k.tc_split = atoi(e) != 0;
         k.trace = getenv("VKBLAS_TRACE") != nullptr;
         return k;
     }();
@@ -73,8 +76,9 @@ struct DeviceState {
     int cc_major = 0, cc_minor = 0;
     int* d_status = nullptr;
     std::mutex mu;
-    // [0]: GEMV split-K (partials + zero-initialised tickets), [1]: 3xTF32 operand planes.
-    std::unordered_map<cudaStream_t, Workspace> ws[2];
+    // [0]: GEMV split-K (partials + zero-initialised tickets), [1]: 3xTF32 operand planes,
+    // [2]: tcgen05 split-K partial tiles.
+    std::unordered_map<cudaStream_t, Workspace> ws[3];
 };
 
 std::mutex g_dev_mu;
@@ -132,6 +136,7 @@ struct ThreadState {
     int path = VKBLAS_PATH_AUTO;
     int splitk = 0;
     int last = VKBLAS_PATH_AUTO;
+    int last_split = 1;
     int test_stall = 0;
 };
 thread_local ThreadState tls;
@@ -178,7 +183,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     if (!path) return VKBLAS_ERR_FALLBACK;
 
     cudaError_t e = cudaSuccess;
-    int splitk = 0;
+    int splitk = 0, split_used = 1;
     if (path == VKBLAS_PATH_GEMV) {
         splitk = tls.splitk > 0 ? tls.splitk : cfg.gemv_splitk > 0 ? cfg.gemv_splitk
                                                                    : gemv_auto_splitk(p, ds->num_sms);
@@ -190,9 +195,11 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
             if (!ws) splitk = 1;
         }
         e = launch_gemv(p, splitk, ws, ds->d_status, s);
+        split_used = splitk;
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
             cudaGetLastError();
             path = VKBLAS_PATH_SIMT;       // weights TMA cannot describe: exact SIMT path
+            split_used = 1;
             e = launch_simt_gemm(p, s);
         } else if (e == cudaErrorNotSupported) {
             cudaGetLastError();
@@ -201,10 +208,16 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     } else if (path == VKBLAS_PATH_TC) {
         const size_t need = umma_workspace_bytes(p);
         void* ws = need ? workspace(ds, 1, s, need) : nullptr;
-        e = (need && !ws) ? cudaErrorNotSupported : launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, tls.test_stall != 0, s);
+        const size_t need_split = cfg.tc_split ? umma_split_workspace_bytes(p, ds->num_sms) : 0;
+        void* wsplit = need_split ? workspace(ds, 2, s, need_split) : nullptr;   // null: no split
+        e = (need && !ws) ? cudaErrorNotSupported
+                          : launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, wsplit,
+                                             tls.test_stall != 0, s);
+        split_used = wsplit ? umma_split_count(p, ds->num_sms) : 1;
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
             cudaGetLastError();
             path = VKBLAS_PATH_SIMT;       // operands TMA cannot describe: exact SIMT path
+            split_used = 1;
             e = launch_simt_gemm(p, s);
         } else if (e == cudaErrorNotSupported) {
             cudaGetLastError();
@@ -224,6 +237,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
                                                                                  : VKBLAS_ERR_INIT;
     }
     tls.last = path;
+    tls.last_split = split_used;
     return VKBLAS_OK;
 }
 
@@ -341,6 +355,7 @@ VKB_EXPORT void vkblas_b200_set_path(int path) {
 }
 VKB_EXPORT int vkblas_b200_get_path(void) { return tls.path; }
 VKB_EXPORT int vkblas_b200_last_path(void) { return tls.last; }
+VKB_EXPORT int vkblas_b200_last_split(void) { return tls.last_split; }
 VKB_EXPORT void vkblas_b200_set_splitk(int splitk) {
     tls.splitk = splitk < 0 ? 0 : splitk > 16 ? 16 : splitk;
 }

@@ -61,6 +61,10 @@ struct __align__(64) UmmaParams {
     int64_t sc;
     uint32_t M, N, K, batch;
     uint32_t tiles_m, tiles_n, num_kb, total_tiles;
+    // Work units: tiles [0, full_tiles) whole; every later tile cut into
+    // split_s K ranges of split_kb k-blocks (stream-K tail / split-K).
+    uint32_t full_tiles, split_s, split_kb, total_units;
+    float* partial;              // [(total_tiles - full_tiles) * split_s][BN][BM] fp32
     uint32_t a_batched, b_batched;
     float alpha, beta;
     const float* d_alpha;
@@ -94,6 +98,25 @@ __device__ __forceinline__ void tile_coords(const UmmaParams& p, uint32_t t, uin
 
 // Epilogue of 32 consecutive outputs of one row: C = alpha*v + beta*C (C not
 // read when beta == 0), converted to T; 128-bit accesses when aligned.
+constexpr uint32_t NO_SPLIT = 0xFFFFFFFFu;
+
+// Work unit u -> (tile, split index or NO_SPLIT, k-block range).
+__device__ __forceinline__ void unit_info(const UmmaParams& p, uint32_t u, uint32_t& tile,
+                                          uint32_t& sp, uint32_t& kb0, uint32_t& kb1) {
+    if (u < p.full_tiles) {
+        tile = u;
+        sp = NO_SPLIT;
+        kb0 = 0;
+        kb1 = p.num_kb;
+    } else {
+        const uint32_t v = u - p.full_tiles;
+        tile = p.full_tiles + v / p.split_s;
+        sp = v % p.split_s;
+        kb0 = sp * p.split_kb;
+        kb1 = min(p.num_kb, kb0 + p.split_kb);
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ void store_row32(T* crow, const float (&v)[32], uint32_t ncols,
                                             bool vec, float alpha, float beta) {
@@ -195,9 +218,6 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // K segments per tile (one when the accumulator is not segmented).
-    const uint32_t seg_kb = C_::SEG_KB ? C_::SEG_KB : p.num_kb;
-    const uint32_t nseg = (p.num_kb + seg_kb - 1) / seg_kb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -228,6 +248,9 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Let a programmatically dependent split_reduce_kernel get resident; it
+    // waits (griddepcontrol.wait) until this grid has finished and flushed.
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
@@ -235,19 +258,20 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_parity = 0;   // per stage: issued ever / last parity
             bool ok = true;
-            for (uint32_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
-                uint32_t b, mb, nb;
+            for (uint32_t u = blockIdx.x; ok && u < p.total_units; u += gridDim.x) {
+                uint32_t t, sp, ukb0, ukb1, b, mb, nb;
+                unit_info(p, u, t, sp, ukb0, ukb1);
                 tile_coords(p, t, b, mb, nb);
                 const int32_t m0 = (int32_t)(mb * BM), n0 = (int32_t)(nb * BN);
                 const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
-                for (uint32_t kb = 0; kb < p.num_kb; kb++) {
+                for (uint32_t kb = ukb0; kb < ukb1; kb++) {
                     if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
                                   DS_TIMEOUT_PRODUCER, p.wait_limit_ns)) {
                         ok = false;
                         break;
                     }
                     const uint32_t fb = full_bar(stage);
-                    if (p.test_skip_first_load && t == blockIdx.x && kb == 0) {
+                    if (p.test_skip_first_load && u == blockIdx.x && kb == ukb0) {
                         // Test hook: leave this stage empty so its consumer's
                         // bounded wait runs out (no copy is issued).
                         if (++stage == STAGES) {
@@ -298,7 +322,11 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
         if (lane == 0) {
             uint32_t stage = 0, phase = 0, u = 0;          // u: accumulator hand-overs so far
             bool ok = true;
-            for (uint32_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+            for (uint32_t w = blockIdx.x; ok && w < p.total_units; w += gridDim.x) {
+                uint32_t t, sp, ukb0, ukb1;
+                unit_info(p, w, t, sp, ukb0, ukb1);
+                const uint32_t seg_kb = C_::SEG_KB ? C_::SEG_KB : (ukb1 - ukb0);
+                const uint32_t nseg = (ukb1 - ukb0 + seg_kb - 1) / seg_kb;
                 for (uint32_t sg = 0; ok && sg < nseg; sg++, u++) {
                     const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
                     if (!wait_bar(tempty_bar(buf), bph ^ 1u, abort_flag, p.status, DS_TIMEOUT_MMA,
@@ -308,8 +336,8 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                     }
                     tc_fence_after();
                     const uint32_t d = tmem_base + buf * BN;
-                    const uint32_t kb0 = sg * seg_kb;
-                    const uint32_t kb1 = min(p.num_kb, kb0 + seg_kb);
+                    const uint32_t kb0 = ukb0 + sg * seg_kb;
+                    const uint32_t kb1 = min(ukb1, kb0 + seg_kb);
                     for (uint32_t kb = kb0; kb < kb1; kb++) {
                         if (!wait_bar(full_bar(stage), phase, abort_flag, p.status, DS_TIMEOUT_MMA,
                                       p.wait_limit_ns)) {
@@ -363,10 +391,21 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
         const uint32_t row = q * 32u + (uint32_t)lane;
         const uint32_t lane_off = (q * 32u) << 16;
         TOut* Cbase = reinterpret_cast<TOut*>(p.C);
-        uint32_t u = 0;
+        uint32_t u = 0;                                       // accumulator hand-overs
         bool ok = true;
-        for (uint32_t t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
-            uint32_t b, mb, nb;
+        // A split unit writes its fp32 partial tile to the workspace and no C;
+        // split_reduce_kernel adds the splits in order and writes C.  Partial
+        // tiles are stored column by column ([BN][BM], row fastest): lane =
+        // row, so for each column a warp writes one contiguous 128-byte line.
+        auto split_publish = [&](uint32_t t, uint32_t sp, const float (&v)[32], int c) {
+            float* P = p.partial + ((size_t)(t - p.full_tiles) * p.split_s + sp) * BM * BN +
+                       (size_t)(col0 + c * 32) * BM + row;
+#pragma unroll
+            for (int i = 0; i < 32; i++) __stcg(P + i * BM, v[i]);
+        };
+        for (uint32_t w = blockIdx.x; ok && w < p.total_units; w += gridDim.x) {
+            uint32_t t, sp, ukb0, ukb1, b, mb, nb;
+            unit_info(p, w, t, sp, ukb0, ukb1);
             tile_coords(p, t, b, mb, nb);
             const uint32_t m = mb * BM + row;
             TOut* crow = Cbase + p.sc * (int64_t)b + (size_t)m * p.ldc;
@@ -382,16 +421,22 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(tmem_base + lane_off + buf * BN + col0 + c * 32, r);
                     tmem_wait_ld();
-                    const uint32_t n0 = nb * BN + col0 + c * 32;
-                    if (m < p.M && n0 < p.N)
-                        store_row32<TOut>(crow + n0, reinterpret_cast<const float(&)[32]>(r),
-                                          min(32u, p.N - n0), p.c_vec_ok != 0, alpha, beta);
+                    const float(&v)[32] = reinterpret_cast<const float(&)[32]>(r);
+                    if (sp != NO_SPLIT) {
+                        split_publish(t, sp, v, c);
+                    } else {
+                        const uint32_t n0 = nb * BN + col0 + c * 32;
+                        if (m < p.M && n0 < p.N)
+                            store_row32<TOut>(crow + n0, v, min(32u, p.N - n0), p.c_vec_ok != 0,
+                                              alpha, beta);
+                    }
                 }
                 tc_fence_before();
                 mbar_arrive(tempty_bar(buf));
                 u++;
             } else {
                 float sum[C_::EPI_COLS / 32][32];
+                const uint32_t nseg = (ukb1 - ukb0 + C_::SEG_KB - 1) / C_::SEG_KB;
                 for (uint32_t sg = 0; sg < nseg; sg++, u++) {
                     const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
                     ok = wait_bar(tfull_bar(buf), bph, abort_flag, p.status, DS_TIMEOUT_EPILOGUE,
@@ -415,10 +460,14 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                 if (!ok) break;
 #pragma unroll
                 for (int c = 0; c < C_::EPI_COLS / 32; c++) {
-                    const uint32_t n0 = nb * BN + col0 + c * 32;
-                    if (m < p.M && n0 < p.N)
-                        store_row32<TOut>(crow + n0, sum[c], min(32u, p.N - n0), p.c_vec_ok != 0,
-                                          alpha, beta);
+                    if (sp != NO_SPLIT) {
+                        split_publish(t, sp, sum[c], c);
+                    } else {
+                        const uint32_t n0 = nb * BN + col0 + c * 32;
+                        if (m < p.M && n0 < p.N)
+                            store_row32<TOut>(crow + n0, sum[c], min(32u, p.N - n0),
+                                              p.c_vec_ok != 0, alpha, beta);
+                    }
                 }
             }
         }
@@ -428,6 +477,69 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C_::TMEM_COLS);
+    }
+}
+
+// Split tiles: C = alpha * (sum of the splits' partials in split order, fp32
+// round-to-nearest) + beta * C.  One 32 x 8 block per 32-row x 64-column chunk:
+// each thread issues the loads of up to four splits together (about S / 4
+// round trips), the chunk is transposed through shared memory and written along C's
+// rows.  Launched as a programmatic dependent of the GEMM grid that wrote the
+// partials.
+template <typename TOut, int BN>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant__ UmmaParams p) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    constexpr uint32_t RC = 32, CC = 64;                // chunk rows x columns
+    constexpr uint32_t CM = BM / RC, CN = BN / CC;
+    __shared__ float tile[CC][RC + 1];                  // [column][row]
+    const uint32_t st = blockIdx.x / (CM * CN);          // split tile
+    const uint32_t r = blockIdx.x - st * (CM * CN);
+    const uint32_t cm = r % CM, cn = r / CM;
+    uint32_t b, mb, nb;
+    tile_coords(p, p.full_tiles + st, b, mb, nb);
+    float alpha = p.alpha, beta = p.beta;
+    load_scalars(p.d_alpha, p.d_beta, alpha, beta);
+    const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const float* P = p.partial + (size_t)st * p.split_s * BM * BN +
+                     (size_t)(cn * CC + ty) * BM + cm * RC + tx;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[j] = __ldcg(P + (size_t)j * 8 * BM);
+    uint32_t q = 1;
+    for (; q + 4 <= p.split_s; q += 4) {                // 32 loads in flight, added in order
+        float x[4][8];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) x[i][j] = __ldcg(P + (size_t)(q + i) * BM * BN + (size_t)j * 8 * BM);
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], x[i][j]);
+    }
+    for (; q < p.split_s; q++) {
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) x[j] = __ldcg(P + (size_t)q * BM * BN + (size_t)j * 8 * BM);
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], x[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) tile[ty + 8 * j][tx] = acc[j];
+    __syncthreads();
+    TOut* C = reinterpret_cast<TOut*>(p.C) + p.sc * (int64_t)b;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t rl = ty + 8 * j, m = mb * BM + cm * RC + rl;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t cl = h * 32 + tx, n = nb * BN + cn * CC + cl;
+            if (m < p.M && n < p.N) {
+                TOut* c = C + (size_t)m * p.ldc + n;
+                const float old = beta != 0.f ? Elem<TOut>::to_f(*c) : 0.f;
+                *c = Elem<TOut>::from_f(epilogue(alpha, tile[cl][rl], beta, old));
+            }
+        }
     }
 }
 
@@ -444,6 +556,8 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, uint32_t rows, 
                                   uint32_t ld, int64_t bstride, uint32_t nb, uint32_t ldo,
                                   float* __restrict__ big, float* __restrict__ small) {
     const uint64_t total = (uint64_t)nb * rows * (ldo / 4);
+    const bool vec_in = (ld & 3u) == 0 && (bstride & 3) == 0 &&
+                        (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
          i += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t br = i / (ldo / 4);
@@ -451,8 +565,13 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, uint32_t rows, 
         const uint32_t b = (uint32_t)(br / rows), r = (uint32_t)(br - (uint64_t)b * rows);
         const float* s = src + bstride * (int64_t)b + (size_t)r * ld;
         float x[4], hi[4], lo[4];
+        if (vec_in && c0 + 3 < cols) {
+            const float4 q = __ldg(reinterpret_cast<const float4*>(s + c0));
+            x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; j++) x[j] = (c0 + j < cols) ? __ldg(s + c0 + j) : 0.f;
+            for (int j = 0; j < 4; j++) x[j] = (c0 + j < cols) ? __ldg(s + c0 + j) : 0.f;
+        }
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             hi[j] = rn_tf32(x[j]);
@@ -466,29 +585,56 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, uint32_t rows, 
 }
 
 // Same split for an MN-major operand (src[b][k][ld], MN contiguous), written
-// K-major (out[b][mn][ldo], K contiguous) through a 32x32 shared-memory tile,
-// so that the tf32 MMAs always read K-major operands.
-__global__ void split_tf32_t_kernel(const float* __restrict__ src, uint32_t K, uint32_t MN,
-                                    uint32_t ld, int64_t bstride, uint32_t nb, uint32_t ldo,
-                                    float* __restrict__ big, float* __restrict__ small) {
-    __shared__ float tile[32][33];
-    const uint32_t mn0 = blockIdx.x * 32u, k0 = blockIdx.y * 32u;
+// K-major (out[b][mn][ldo], K contiguous) so that the tf32 MMAs always read
+// K-major operands.  A 64x64 tile goes through shared memory; both the global
+// reads (along MN) and the writes (along K) are 128-bit when aligned.
+constexpr int TT = 64;
+__global__ void __launch_bounds__(256) split_tf32_t_kernel(const float* __restrict__ src,
+                                                           uint32_t K, uint32_t MN, uint32_t ld,
+                                                           int64_t bstride, uint32_t nb,
+                                                           uint32_t ldo, float* __restrict__ big,
+                                                           float* __restrict__ small) {
+    __shared__ float tile[TT][TT + 1];                // [k][mn]
+    const uint32_t mn0 = blockIdx.x * TT, k0 = blockIdx.y * TT;
+    const uint32_t tx = threadIdx.x & 15, ty = threadIdx.x >> 4;    // 16 x 16
+    const bool vec_in = (ld & 3u) == 0 && (bstride & 3) == 0 &&
+                        (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
     for (uint32_t b = blockIdx.z; b < nb; b += gridDim.z) {
         const float* s = src + bstride * (int64_t)b;
-        for (uint32_t i = threadIdx.y; i < 32u; i += 8u) {
-            const uint32_t k = k0 + i, mn = mn0 + threadIdx.x;
-            tile[i][threadIdx.x] = (k < K && mn < MN) ? __ldg(s + (size_t)k * ld + mn) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t kl = ty + 16 * i, k = k0 + kl, mn = mn0 + tx * 4;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (k < K) {
+                const float* row = s + (size_t)k * ld;
+                if (vec_in && mn + 3 < MN) {
+                    const float4 q = __ldg(reinterpret_cast<const float4*>(row + mn));
+                    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if (mn + j < MN) v[j] = __ldg(row + mn + j);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++) tile[kl][tx * 4 + j] = v[j];
         }
         __syncthreads();
         const size_t obase = (size_t)b * MN * ldo;
-        for (uint32_t i = threadIdx.y; i < 32u; i += 8u) {
-            const uint32_t mn = mn0 + i, k = k0 + threadIdx.x;
-            if (mn < MN && k < ldo) {
-                const float x = tile[threadIdx.x][i];
-                const float hi = rn_tf32(x);
-                const float lo = isfinite(hi) ? rn_tf32(x - hi) : 0.f;
-                big[obase + (size_t)mn * ldo + k] = hi;
-                small[obase + (size_t)mn * ldo + k] = lo;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t ml = ty + 16 * i, mn = mn0 + ml, k = k0 + tx * 4;
+            if (mn < MN && k < ldo) {                  // ldo % 4 == 0: k..k+3 < ldo
+                float hi[4], lo[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float x = tile[tx * 4 + j][ml];
+                    hi[j] = rn_tf32(x);
+                    lo[j] = isfinite(hi[j]) ? rn_tf32(x - hi[j]) : 0.f;
+                }
+                const size_t o = obase + (size_t)mn * ldo + k;
+                *reinterpret_cast<float4*>(big + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(small + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
             }
         }
         __syncthreads();
@@ -597,8 +743,70 @@ cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, int grid,
     return launch_kind<KIND, true, true, BN, STAGES>(prm, grid, s);
 }
 
+// The reduce of split tiles, launched so that it may become resident while
+// the GEMM grid drains (programmatic stream serialization).
+template <typename TOut, int BN>
+cudaError_t launch_reduce(const UmmaParams& prm, cudaStream_t s) {
+    const uint32_t chunks = (prm.total_tiles - prm.full_tiles) * (BM / 32) * (BN / 64);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(chunks);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, split_reduce_kernel<TOut, BN>, prm);
+    count_launch();
+    return e;
+}
+
 constexpr int BN_16 = 256, STAGES_16 = 4;
 constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
+
+// Work decomposition.  Whole waves of tiles run unsplit; the tiles of the
+// last, partial wave (all tiles when there are fewer tiles than SMs -- the
+// reference's skinny split-K case, src/vkblas.c:2850-2867) are cut along K
+// into S ranges so that the last wave fills the GPU, when that saves more
+// than the split costs: the partial tiles make a round trip through L2 and a
+// second kernel adds them (measured on B200: about 10 us for a wave of
+// 128 x 256 tiles), so at least MIN_SAVED_KB k-blocks of a tile's MMA time
+// (about 0.37 us each for fp16, 0.7 us for 3xTF32) must go.
+struct SplitPlan {
+    uint32_t full, s, kb_per, units;
+    size_t partial_bytes;
+};
+
+SplitPlan plan_split(const GemmProblem& p, int num_sms) {
+    const bool is32 = p.dtype == DT_F32;
+    const uint32_t BN = is32 ? BN_TF32 : BN_16;
+    const uint32_t BK = ROW_BYTES / (is32 ? 4u : 2u);
+    const uint32_t seg = is32 ? 8u : 1u;                // 3xTF32 accumulates 8-k-block segments
+    const uint32_t min_saved_kb = is32 ? 16u : 48u;
+    const uint64_t T = (uint64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN) * p.batch;
+    const uint32_t num_kb = (p.K + BK - 1) / BK;
+    SplitPlan pl{(uint32_t)T, 1, num_kb, (uint32_t)T, 0};
+    const uint64_t P = (uint64_t)(num_sms > 0 ? num_sms : 1);
+    const uint64_t rem = T % P;
+    if (rem == 0 || T >= (1ull << 31)) return pl;
+    uint32_t S = (uint32_t)(P / rem);
+    if (S > 16) S = 16;
+    const uint32_t min_kb = seg > 4 ? seg : 4;
+    if (S > num_kb / min_kb) S = num_kb / min_kb;
+    if (S < 2) return pl;
+    uint32_t kb_per = (num_kb + S - 1) / S;
+    kb_per = (kb_per + seg - 1) / seg * seg;
+    const uint32_t s2 = (num_kb + kb_per - 1) / kb_per;
+    if (s2 < 2 || num_kb - kb_per < min_saved_kb) return pl;
+    pl.full = (uint32_t)(T - rem);
+    pl.s = s2;
+    pl.kb_per = kb_per;
+    pl.units = pl.full + (uint32_t)rem * s2;
+    pl.partial_bytes = (size_t)rem * s2 * BM * BN * sizeof(float);
+    return pl;
+}
 
 }  // namespace
 
@@ -632,6 +840,13 @@ bool umma_profitable(const GemmProblem& p) {
     return (uint64_t)p.M * p.N * p.K >= (1ull << 21) && p.M >= 32 && p.N >= 32;
 }
 
+int umma_split_count(const GemmProblem& p, int num_sms) { return (int)plan_split(p, num_sms).s; }
+
+size_t umma_split_workspace_bytes(const GemmProblem& p, int num_sms) {
+    const SplitPlan pl = plan_split(p, num_sms);
+    return pl.s > 1 ? pl.partial_bytes : 0;
+}
+
 size_t umma_workspace_bytes(const GemmProblem& p) {
     if (p.dtype != DT_F32) return 0;
     const uint64_t a = plane_elems(operand_a(p)), b = plane_elems(operand_b(p));
@@ -640,7 +855,7 @@ size_t umma_workspace_bytes(const GemmProblem& p) {
 }
 
 cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* ws,
-                             bool test_stall, cudaStream_t s) {
+                             void* split_ws, bool test_stall, cudaStream_t s) {
     UmmaParams prm;
     memset(&prm, 0, sizeof(prm));
     prm.wait_limit_ns = test_stall ? TEST_WAIT_LIMIT_NS : WAIT_LIMIT_NS;
@@ -696,9 +911,9 @@ cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, v
                     reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
                     (uint32_t)o.ld, (int64_t)o.bstride, (uint32_t)o.nb, ldo, big, small);
             } else {
-                dim3 grid((uint32_t)((o.inner + 31) / 32), (uint32_t)((o.outer + 31) / 32),
+                dim3 grid((uint32_t)((o.inner + TT - 1) / TT), (uint32_t)((o.outer + TT - 1) / TT),
                           (uint32_t)(o.nb < 65535 ? o.nb : 65535));
-                split_tf32_t_kernel<<<grid, dim3(32, 8), 0, s>>>(
+                split_tf32_t_kernel<<<grid, 256, 0, s>>>(
                     reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
                     (uint32_t)o.ld, (int64_t)o.bstride, (uint32_t)o.nb, ldo, big, small);
             }
@@ -719,20 +934,41 @@ cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, v
     const uint64_t total = (uint64_t)prm.tiles_m * prm.tiles_n * p.batch;
     if (total >= (1ull << 31)) return cudaErrorNotSupported;
     prm.total_tiles = (uint32_t)total;
+    const SplitPlan pl = plan_split(p, num_sms);
+    if (pl.s > 1 && split_ws) {
+        prm.full_tiles = pl.full;
+        prm.split_s = pl.s;
+        prm.split_kb = pl.kb_per;
+        prm.total_units = pl.units;
+        prm.partial = reinterpret_cast<float*>(split_ws);
+    } else {
+        prm.full_tiles = prm.total_tiles;
+        prm.split_s = 1;
+        prm.split_kb = prm.num_kb;
+        prm.total_units = prm.total_tiles;
+    }
     prm.a_batched = a.nb > 1;
     prm.b_batched = b.nb > 1;
     prm.alpha = p.alpha; prm.beta = p.beta; prm.d_alpha = p.d_alpha; prm.d_beta = p.d_beta;
     prm.status = d_status;
     prm.c_vec_ok = al16(p.C) && ((uint64_t)p.ldc * esize) % 16 == 0 &&
                    (p.batch == 1 || ((uint64_t)p.sc * esize) % 16 == 0);
-    const int grid = (int)(total < (uint64_t)num_sms ? total : (uint64_t)num_sms);
+    const int grid = (int)(prm.total_units < (uint32_t)num_sms ? prm.total_units : (uint32_t)num_sms);
     const bool amn = a.mn_major, bmn = b.mn_major;
+    cudaError_t e;
     switch (p.dtype) {
-        case DT_F16: return launch_majors<K_F16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
-        case DT_BF16: return launch_majors<K_BF16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
+        case DT_F16: e = launch_majors<K_F16, BN_16, STAGES_16>(amn, bmn, prm, grid, s); break;
+        case DT_BF16: e = launch_majors<K_BF16, BN_16, STAGES_16>(amn, bmn, prm, grid, s); break;
         case DT_F32:   // planes are K-major whatever op(A), op(B) are
-            return launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32>(prm, grid, s);
+            e = launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32>(prm, grid, s);
+            break;
         default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess || prm.split_s <= 1) return e;
+    switch (p.dtype) {
+        case DT_F16: return launch_reduce<__half, BN_16>(prm, s);
+        case DT_BF16: return launch_reduce<__nv_bfloat16, BN_16>(prm, s);
+        default: return launch_reduce<float, BN_TF32>(prm, s);
     }
 }
 
