@@ -167,8 +167,8 @@ def secondary_results(vk, hb, torch, peaks):
     g = torch.Generator(device="cuda").manual_seed(3)
     with hb.Handle() as h, torch.cuda.stream(s):
         h.set_stream(s)
-        # config 3: HGEMM T/N 4096^3 and 8192^3
-        for n in (4096, 8192):
+        # config 3: HGEMM T/N 4096^3, 8192^3 and 16384^3
+        for n in (4096, 8192, 16384):
             sets = [((torch.randn(n, n, device="cuda", generator=g) * 0.02).half(),
                      (torch.randn(n, n, device="cuda", generator=g) * 0.02).half(),
                      torch.empty(n, n, device="cuda", dtype=torch.float16)) for _ in range(2)]
@@ -181,7 +181,7 @@ def secondary_results(vk, hb, torch, peaks):
                                         vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
             for i in range(3):
                 run(i)
-            ms = _time_loop(run, 10 if n == 4096 else 4, s)
+            ms = _time_loop(run, {4096: 10, 8192: 4, 16384: 2}[n], s)
             tf = 2.0 * n ** 3 / ms / 1e9
             out[f"hgemm_tn_{n}"] = {"tflops": round(tf, 2), "ms": round(ms, 4),
                                     "path": vk.PATH_NAMES[vk.last_path()],
@@ -237,6 +237,40 @@ def secondary_results(vk, hb, torch, peaks):
                                          "path": vk.PATH_NAMES[vk.last_path()],
                                          "frac_of_bf16_burst": round(tf / peaks["bf16_tflops"], 4)}
         del A, B, C
+    return out
+
+
+def sharded_config5(vk, torch, dist, rank, world, stream):
+    """BASELINE config 5 across the ranks: 256 x 2048^3 fp16 NN strided-batched,
+    sharded by batch (weak in the number of GEMMs per rank), timed without and
+    with the all-gather that replicates C (2 GiB) on every rank; max over ranks."""
+    from vkblas_b200 import shard
+    b, n = 256, 2048
+    b0, cnt = shard.batch_shard(b, rank, world)
+    g = torch.Generator(device="cuda").manual_seed(500 + rank)
+    A = (torch.randn(cnt * n * n, device="cuda", generator=g) * 0.02).half()
+    B = (torch.randn(cnt * n * n, device="cuda", generator=g) * 0.02).half()
+    C_full = torch.empty(b * n * n, device="cuda", dtype=torch.float16)
+    C_local = C_full[b0 * n * n: (b0 + cnt) * n * n]
+
+    def run(gather):
+        shard.sharded_batched_gemm(vk.DT_F16, 0, 0, n, n, n, 1.0, A, n, n * n, B, n, n * n, 0.0,
+                                   C_local, n, n * n, b, rank=rank, world=world,
+                                   C_full=C_full if gather else None)
+    out = {}
+    for gather in (False, True):
+        run(gather)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms = _time_loop(lambda i: run(gather), 3, stream)
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        key = "with_allgather" if gather else "gemm_only"
+        out[key] = {"ms": round(ms, 3), "tflops": round(b * 2.0 * n ** 3 / ms / 1e9, 2)}
+    out["allgather_ms"] = round(out["with_allgather"]["ms"] - out["gemm_only"]["ms"], 3)
+    out["allgather_bytes"] = b * n * n * 2
+    del A, B, C_full, C_local
     return out
 
 
@@ -399,6 +433,11 @@ def main() -> int:
             result["secondary"] = secondary_results(vk, hb, torch, peaks)
         except Exception as exc:   # secondary numbers never hide the headline
             result["secondary"] = {"error": repr(exc)}
+    if world > 1 and not args.no_secondary:
+        # every rank takes the same collective steps; an error ends the run
+        result["secondary"] = {"hgemm_batched_256x2048_sharded": sharded_config5(
+            vk, torch, dist, rank, world, stream)}
+        torch.cuda.empty_cache()
     h.close()
     if world > 1:
         dist.barrier()

@@ -26,8 +26,11 @@
  *     (test/test_h.c:23-41, ties rounded up) -- the exact pin of cpu_ref.
  *   - orc_hgemm_rowmajor_splitk: split-K semantics of the reference's
  *     matvec/split-K family (matvec_splitk_tmpl.comp:64-79,
- *     splitk_reduce_half.comp:16-35): per-segment fp32 partial sums, added in
- *     segment order, then alpha/beta and RNE.
+ *     splitk_reduce_half.comp:22-35): per-segment fp32 partial sums, added in
+ *     segment order, then alpha/beta and the store encoder: RNE (rounding 0,
+ *     what this library's kernels do), or the reference reduce's own encoders
+ *     (rounding 1: packHalf2x16 RNE for fp16, truncation to the upper 16 bits
+ *     for bf16 -- splitk_reduce_half.comp:5,8, splitk_reduce_m_half.comp:6,9).
  *   - f16/bf16 converters: exact RNE (what packHalf2x16 and the GPU's
  *     __float2half_rn do) plus a replica of test/test_h.c:16-41's own
  *     encoders, which the reference's tests use to build their inputs.
@@ -230,10 +233,18 @@ EXPORT void orc_hgemm_rowmajor(int dtype, int acc_mode, int op_a, int op_b,
 
 /* Split-K model: K cut into nseg segments of ceil(K/nseg); each segment is a
  * sequential fp32 sum; segment partials are added in segment order. */
+static inline uint16_t narrow_reduce_ref(int dtype, float v) {
+    if (!dtype) return orc_f2h_rne(v);
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    return (uint16_t)(u >> 16);          /* splitk_reduce_half.comp:8 */
+}
+
 EXPORT void orc_hgemm_rowmajor_splitk(int dtype, int op_a, int op_b, uint32_t M, uint32_t N,
                                       uint32_t K, uint32_t nseg, float alpha,
                                       const uint16_t* A, uint32_t lda, const uint16_t* B,
-                                      uint32_t ldb, float beta, uint16_t* C, uint32_t ldc) {
+                                      uint32_t ldb, float beta, uint16_t* C, uint32_t ldc,
+                                      int rounding) {
     uint32_t span = (K + nseg - 1) / nseg;
     for (uint32_t m = 0; m < M; m++)
         for (uint32_t n = 0; n < N; n++) {
@@ -250,7 +261,7 @@ EXPORT void orc_hgemm_rowmajor_splitk(int dtype, int op_a, int op_b, uint32_t M,
             float old = beta != 0.0f ? widen(dtype, *c) : 0.0f;
             float t1 = alpha * total;
             float t2 = beta * old;
-            *c = narrow(dtype, t1 + t2);
+            *c = rounding ? narrow_reduce_ref(dtype, t1 + t2) : narrow(dtype, t1 + t2);
         }
 }
 

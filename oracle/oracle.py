@@ -50,7 +50,7 @@ def _load():
     lib.orc_hgemm_rowmajor.argtypes = [_i, _i, _i, _i, _u32, _u32, _u32, _f, _u16p, _u32, _u16p, _u32,
                                        _f, _u16p, _u32, _u32, _i64, _i64, _i64]
     lib.orc_hgemm_rowmajor_splitk.argtypes = [_i, _i, _i, _u32, _u32, _u32, _u32, _f, _u16p, _u32,
-                                              _u16p, _u32, _f, _u16p, _u32]
+                                              _u16p, _u32, _f, _u16p, _u32, _i]
     lib.orc_gen_test_gemm.argtypes = [C.c_uint, _f32p, _sz, _f32p, _sz, _f32p, _sz]
     lib.orc_gen_test_h.argtypes = [C.c_uint, _i, _u16p, _sz, _u16p, _sz, _u16p, _sz, _i]
     lib.orc_sgemm_colmajor_rows_mt.argtypes = [_i, _i, _i, _i, _i, _f, _f32p, _i, _f32p, _i, _f,
@@ -154,8 +154,13 @@ def hgemm_rowmajor_f64(dtype, op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, 
                              None if Cf is None else np.ascontiguousarray(Cf), ldc, batch, sa, sb, sc)
 
 
-def hgemm_rowmajor_splitk(dtype, op_a, op_b, M, N, K, nseg, alpha, A, lda, B, ldb, beta, C, ldc):
-    lib.orc_hgemm_rowmajor_splitk(dtype, op_a, op_b, M, N, K, nseg, alpha, A, lda, B, ldb, beta, C, ldc)
+def hgemm_rowmajor_splitk(dtype, op_a, op_b, M, N, K, nseg, alpha, A, lda, B, ldb, beta, C, ldc,
+                          rounding=0):
+    """Segmented fp32 sums added in order, alpha/beta, then the store encoder:
+    rounding 0 = RNE (this library), 1 = the reference reduce's encoders
+    (bf16 truncated, splitk_reduce_half.comp:8)."""
+    lib.orc_hgemm_rowmajor_splitk(dtype, op_a, op_b, M, N, K, nseg, alpha, A, lda, B, ldb, beta, C, ldc,
+                                  rounding)
 
 
 # -------------------------------------------------------------- generators

@@ -38,8 +38,10 @@ def _worker(rank, world, port, kind):
     rng = np.random.default_rng(99)
     try:
         if kind == "batch":
-            batch, M, N, K = 7, 24, 20, 16
-            for bcast in (None, "a"):
+            M, N, K = 24, 20, 16
+            # batch 7: uneven shards (padded gather); batch 8: equal shards, C
+            # computed in place in this rank's slice of the replicated C
+            for batch, bcast in ((7, None), (7, "a"), (8, None)):
                 sa = 0 if bcast == "a" else M * K
                 sb, sc = K * N, M * N
                 A = rng.uniform(-1, 1, (sa * (batch - 1) if sa else 0) + M * K).astype(np.float32)
@@ -50,8 +52,12 @@ def _worker(rank, world, port, kind):
                 b0, n = shard.batch_shard(batch, rank, world)
                 Al = torch.from_numpy(A[b0 * sa: (b0 + n) * sa] if sa else A).clone()
                 Bl = torch.from_numpy(B[b0 * sb: (b0 + n) * sb]).clone()
-                Cl = torch.from_numpy(C0[b0 * sc: (b0 + n) * sc]).clone()
                 full = torch.zeros(sc * batch)
+                if batch % world == 0:
+                    Cl = full[b0 * sc: (b0 + n) * sc]
+                    Cl.copy_(torch.from_numpy(C0[b0 * sc: (b0 + n) * sc]))
+                else:
+                    Cl = torch.from_numpy(C0[b0 * sc: (b0 + n) * sc]).clone()
                 shard.sharded_batched_gemm(0, 0, 0, M, N, K, 1.5, Al, K, sa, Bl, N, sb, 0.5, Cl, N, sc,
                                            batch, rank=rank, world=world, C_full=full,
                                            gemm_fn=_cpu_gemm)

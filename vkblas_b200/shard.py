@@ -74,6 +74,11 @@ def sharded_batched_gemm(dtype: int, op_a: int, op_b: int, M: int, N: int, K: in
         if sc < M * ldc:
             raise ValueError("replicated C needs non-overlapping C batches (sc >= M*ldc)")
         per = max(batch_shard(batch, r, world)[1] for r in range(world))
+        if batch % world == 0:
+            # Equal shards: gather straight into C_full (in place when C_local is
+            # this rank's slice of C_full, as NCCL's in-place all-gather expects).
+            _all_gather_flat(C_full[: batch * sc], C_local[: count * sc], world, group)
+            return begin, count
         shard = torch.zeros(per * sc, dtype=C_local.dtype, device=C_local.device)
         if count:
             shard[: count * sc].copy_(C_local[: count * sc])
