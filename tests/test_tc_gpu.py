@@ -139,3 +139,40 @@ def test_tc_alpha_beta(dtype, cuda):
 @pytest.mark.parametrize("bcast", [None, "a", "b"])
 def test_tc_batched(dtype, bcast, cuda):
     _run(dtype, 0, 0, 160, 136, 96, 1.0, 0.5, batch=3, bcast=bcast)
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_F32], ids=["f16", "f32"])
+def test_tc_split_k_graph_capture(dtype, cuda):
+    """A split call (GEMM + programmatically dependent reduce) captured in a
+    CUDA graph and replayed gives the eager call's result bit for bit."""
+    import torch
+    M, N, K = 256, 384, 8192
+    tdt = torch.float32 if dtype == vk.DT_F32 else torch.float16
+    g = torch.Generator(device="cuda").manual_seed(11)
+    A = torch.randn(M, K, device="cuda", generator=g).to(tdt)
+    B = torch.randn(K, N, device="cuda", generator=g).to(tdt)
+    C_eager = torch.zeros(M, N, device="cuda", dtype=tdt)
+    C_graph = torch.zeros(M, N, device="cuda", dtype=tdt)
+    s = torch.cuda.Stream()
+
+    def call(C):
+        st = vk.gemm(dtype, 0, 0, M, N, K, 0.5, A.data_ptr(), K, B.data_ptr(), N, 0.0,
+                     C.data_ptr(), N)
+        assert st == vk.VKBLAS_OK
+
+    with torch.cuda.stream(s):
+        vk.set_stream(s)
+        call(C_eager)                       # sizes the workspace before capture
+        torch.cuda.synchronize()
+        assert vk.last_split() > 1
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            call(C_graph)
+        for _ in range(2):
+            C_graph.zero_()
+            graph.replay()
+    torch.cuda.synchronize()
+    vk.set_stream(torch.cuda.current_stream())
+    check_status()
+    assert torch.equal(C_graph, C_eager)
+    del graph
