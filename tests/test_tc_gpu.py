@@ -176,3 +176,27 @@ def test_tc_split_k_graph_capture(dtype, cuda):
     check_status()
     assert torch.equal(C_graph, C_eager)
     del graph
+
+
+# Small-M 2-byte GEMMs (decode with up to 64 tokens, N >= 128) run transposed:
+# C^T = op(B)^T op(A)^T with weight rows on the MMA's 128 lanes and the tokens
+# on a 64-wide N tile; the epilogue writes C transposed.  (shape, split)
+SMALL_M_SHAPES = [
+    ((1, 4096, 512), False),
+    ((7, 1000, 520), False),       # ragged N and K
+    ((16, 384, 4096), True),       # 3 weight-row tiles: K split 16 ways
+    ((33, 200, 136), False),
+    ((64, 4096, 4096), True),      # 32 tiles: K split 4 ways
+]
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_BF16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("ops", [(0, 0), (0, 1), (1, 0), (1, 1)], ids=["NN", "NT", "TN", "TT"])
+@pytest.mark.parametrize("case", SMALL_M_SHAPES, ids=[f"{m}x{n}x{k}" for (m, n, k), _ in SMALL_M_SHAPES])
+def test_tc_small_m_transposed(dtype, ops, case, cuda):
+    (M, N, K), split = case
+    _run(dtype, ops[0], ops[1], M, N, K, 0.75, -0.5, split=split)
+
+
+def test_tc_small_m_batched_broadcast(cuda):
+    _run(vk.DT_F16, 0, 1, 12, 640, 256, 1.0, 0.5, batch=3, bcast="b", split=False)

@@ -3,11 +3,12 @@
     python -m vkblas_b200.cases sgemm  [--n 4096] [--shape M,N,K] [--iters 3]   # 3xTF32, N/N
     python -m vkblas_b200.cases sgemm-simt [--n 4096]                # exact FFMA kernel
     python -m vkblas_b200.cases hgemm  [--n 4096] [--shape M,N,K]    # fp16 tcgen05, hipBLAS T/N
-    python -m vkblas_b200.cases gemv   [--m 1] [--splitk 4]          # decode GEMV, K=4096, N=14336
+    python -m vkblas_b200.cases gemv   [--m 1] [--splitk 4]          # decode, K=4096, N=14336, M<=64
     python -m vkblas_b200.cases batched                              # 256 x 2048^3 fp16 N/N
 
 Inputs are device-resident and seeded; each iteration is one library call on
 torch's current stream; the mean time per call (CUDA events) is printed.
+--path simt|tc|gemv forces a kernel family (the call fails if it cannot run).
 """
 from __future__ import annotations
 
@@ -27,6 +28,8 @@ def main(argv=None) -> int:
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--splitk", type=int, default=0)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc", "gemv"],
+                    help="force a kernel family (vkblas_b200_set_path)")
     a = ap.parse_args(argv)
 
     torch.cuda.init()
@@ -59,16 +62,21 @@ def main(argv=None) -> int:
                                                vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
     elif a.case == "gemv":
         K, O, M = 4096, 14336, a.m
-        W = (torch.randn(O * K, device="cuda", generator=g) * 0.02).half()
+        # four weight sets (470 MB > 126 MB L2), rotated call by call
+        Ws = [(torch.randn(O * K, device="cuda", generator=g) * 0.02).half() for _ in range(4)]
         X = torch.randn(M * K, device="cuda", generator=g).half()
         C = torch.empty(M * O, device="cuda", dtype=torch.float16)
         if a.splitk:
             vk.set_splitk(a.splitk)
         flop, nbytes = 2.0 * M * O * K, 2.0 * (O * K + M * K + M * O)
-        call = lambda: vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,  # noqa: E731
-                                            W.data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
-                                            vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F,
-                                            O, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+        turn = [0]
+
+        def call():
+            turn[0] += 1
+            return vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,
+                                        Ws[turn[0] % 4].data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
+                                        vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F, O,
+                                        vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
     else:
         b, n = 256, 2048
         A = (torch.randn(b * n * n, device="cuda", generator=g) * 0.02).half()
@@ -80,6 +88,8 @@ def main(argv=None) -> int:
             n * n, B.data_ptr(), vk.HIP_R_16F, n, n * n, be, C.data_ptr(), vk.HIP_R_16F, n, n * n,
             b, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
 
+    if a.path != "auto":
+        vk.set_path({"simt": vk.PATH_SIMT, "tc": vk.PATH_TC, "gemv": vk.PATH_GEMV}[a.path])
     st = call()
     if st != 0:
         raise SystemExit(f"status {st}")

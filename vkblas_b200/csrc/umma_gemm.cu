@@ -71,6 +71,10 @@ struct __align__(64) UmmaParams {
     const float* d_beta;
     int* status;
     uint32_t c_vec_ok;
+    // C transposed: the kernel computes C^T = op(B)^T op(A)^T (small-M decode
+    // shapes, weight rows on the MMA's 128 lanes) and element (row, col) of
+    // its tile goes to C + col * ldc + row.
+    uint32_t c_trans;
     uint64_t wait_limit_ns;      // bound of every mbarrier wait
     uint32_t test_skip_first_load;   // test hook: the first stage is never filled
 };
@@ -156,6 +160,23 @@ __device__ __forceinline__ void store_row32(T* crow, const float (&v)[32], uint3
                 const float c = (beta != 0.f) ? Elem<T>::to_f(crow[i]) : 0.f;
                 crow[i] = Elem<T>::from_f(epilogue(alpha, v[i], beta, c));
             }
+        }
+    }
+}
+
+// Transposed epilogue: this thread's tile row `row` is a column of C, its 32
+// values go down C's rows n0.. (lanes hold consecutive columns of C, so each
+// store instruction of a warp is contiguous).
+template <typename T>
+__device__ __forceinline__ void store_col32(T* cb, uint32_t row, uint32_t n0, uint32_t ldc,
+                                            const float (&v)[32], uint32_t ncols, float alpha,
+                                            float beta) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        if ((uint32_t)i < ncols) {
+            T* c = cb + (size_t)(n0 + i) * ldc + row;
+            const float old = (beta != 0.f) ? Elem<T>::to_f(*c) : 0.f;
+            *c = Elem<T>::from_f(epilogue(alpha, v[i], beta, old));
         }
     }
 }
@@ -408,7 +429,8 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
             unit_info(p, w, t, sp, ukb0, ukb1);
             tile_coords(p, t, b, mb, nb);
             const uint32_t m = mb * BM + row;
-            TOut* crow = Cbase + p.sc * (int64_t)b + (size_t)m * p.ldc;
+            TOut* cb = Cbase + p.sc * (int64_t)b;
+            TOut* crow = cb + (size_t)m * p.ldc;
             if constexpr (C_::SEG_KB == 0) {
                 const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
                 ok = wait_bar(tfull_bar(buf), bph, abort_flag, p.status, DS_TIMEOUT_EPILOGUE,
@@ -426,9 +448,13 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                         split_publish(t, sp, v, c);
                     } else {
                         const uint32_t n0 = nb * BN + col0 + c * 32;
-                        if (m < p.M && n0 < p.N)
-                            store_row32<TOut>(crow + n0, v, min(32u, p.N - n0), p.c_vec_ok != 0,
-                                              alpha, beta);
+                        if (m < p.M && n0 < p.N) {
+                            if (p.c_trans)
+                                store_col32<TOut>(cb, m, n0, p.ldc, v, min(32u, p.N - n0), alpha, beta);
+                            else
+                                store_row32<TOut>(crow + n0, v, min(32u, p.N - n0), p.c_vec_ok != 0,
+                                                  alpha, beta);
+                        }
                     }
                 }
                 tc_fence_before();
@@ -464,9 +490,14 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                         split_publish(t, sp, sum[c], c);
                     } else {
                         const uint32_t n0 = nb * BN + col0 + c * 32;
-                        if (m < p.M && n0 < p.N)
-                            store_row32<TOut>(crow + n0, sum[c], min(32u, p.N - n0),
-                                              p.c_vec_ok != 0, alpha, beta);
+                        if (m < p.M && n0 < p.N) {
+                            if (p.c_trans)
+                                store_col32<TOut>(cb, m, n0, p.ldc, sum[c], min(32u, p.N - n0),
+                                                  alpha, beta);
+                            else
+                                store_row32<TOut>(crow + n0, sum[c], min(32u, p.N - n0),
+                                                  p.c_vec_ok != 0, alpha, beta);
+                        }
                     }
                 }
             }
@@ -524,10 +555,24 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
 #pragma unroll
         for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], x[j]);
     }
+    TOut* C = reinterpret_cast<TOut*>(p.C) + p.sc * (int64_t)b;
+    if (p.c_trans) {            // lanes run along C's rows already: store directly
+        const uint32_t m = mb * BM + cm * RC + tx;
+        if (m >= p.M) return;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint32_t n = nb * BN + cn * CC + ty + 8 * j;
+            if (n < p.N) {
+                TOut* c = C + (size_t)n * p.ldc + m;
+                const float old = beta != 0.f ? Elem<TOut>::to_f(*c) : 0.f;
+                *c = Elem<TOut>::from_f(epilogue(alpha, acc[j], beta, old));
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int j = 0; j < 8; j++) tile[ty + 8 * j][tx] = acc[j];
     __syncthreads();
-    TOut* C = reinterpret_cast<TOut*>(p.C) + p.sc * (int64_t)b;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         const uint32_t rl = ty + 8 * j, m = mb * BM + cm * RC + rl;
@@ -764,6 +809,36 @@ cudaError_t launch_reduce(const UmmaParams& prm, cudaStream_t s) {
 }
 
 constexpr int BN_16 = 256, STAGES_16 = 4;
+// Small-M 2-byte GEMMs (decode with up to 64 tokens) run transposed: weight
+// rows on the MMA's 128 lanes, tokens on a 64-wide N tile, an 8-deep ring.
+constexpr int BN_SM = 64, STAGES_SM = 8;
+constexpr uint32_t SMALL_M_MAX = 64;
+
+bool small_m_swap(const GemmProblem& p) {
+    return (p.dtype == DT_F16 || p.dtype == DT_BF16) && p.M <= SMALL_M_MAX && p.N >= 128;
+}
+
+// C^T = op(B)^T op(A)^T in the engine's row-major terms: op(B)^T is B read
+// with the opposite transpose flag, and likewise for A.
+GemmProblem swapped(const GemmProblem& p) {
+    GemmProblem q = p;
+    q.M = p.N;
+    q.N = p.M;
+    q.A = p.B; q.lda = p.ldb; q.sa = p.sb; q.op_a = p.op_b ? 0 : 1;
+    q.B = p.A; q.ldb = p.lda; q.sb = p.sa; q.op_b = p.op_a ? 0 : 1;
+    return q;
+}
+
+// The problem the kernel runs and its N tile.
+struct KernelShape {
+    GemmProblem q;
+    bool c_trans;
+    uint32_t BN;
+};
+KernelShape kernel_shape(const GemmProblem& p) {
+    if (small_m_swap(p)) return {swapped(p), true, (uint32_t)BN_SM};
+    return {p, false, (uint32_t)(p.dtype == DT_F32 ? 128 : BN_16)};
+}
 constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
 
 // Work decomposition.  Whole waves of tiles run unsplit; the tiles of the
@@ -779,12 +854,15 @@ struct SplitPlan {
     size_t partial_bytes;
 };
 
-SplitPlan plan_split(const GemmProblem& p, int num_sms) {
+SplitPlan plan_split(const KernelShape& ks, int num_sms) {
+    const GemmProblem& p = ks.q;
     const bool is32 = p.dtype == DT_F32;
-    const uint32_t BN = is32 ? BN_TF32 : BN_16;
+    const uint32_t BN = ks.BN;
     const uint32_t BK = ROW_BYTES / (is32 ? 4u : 2u);
     const uint32_t seg = is32 ? 8u : 1u;                // 3xTF32 accumulates 8-k-block segments
-    const uint32_t min_saved_kb = is32 ? 16u : 48u;
+    // 128 x 64 small-M tiles stream weights (~0.3 us per k-block) and their
+    // partial tiles are a quarter of a 128 x 256 tile's.
+    const uint32_t min_saved_kb = is32 ? 16u : (BN == (uint32_t)BN_SM ? 8u : 48u);
     const uint64_t T = (uint64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN) * p.batch;
     const uint32_t num_kb = (p.K + BK - 1) / BK;
     SplitPlan pl{(uint32_t)T, 1, num_kb, (uint32_t)T, 0};
@@ -837,13 +915,16 @@ bool umma_supported(const GemmProblem& p) {
 }
 
 bool umma_profitable(const GemmProblem& p) {
-    return (uint64_t)p.M * p.N * p.K >= (1ull << 21) && p.M >= 32 && p.N >= 32;
+    if ((uint64_t)p.M * p.N * p.K < (1ull << 21)) return false;
+    return (p.M >= 32 && p.N >= 32) || small_m_swap(p);
 }
 
-int umma_split_count(const GemmProblem& p, int num_sms) { return (int)plan_split(p, num_sms).s; }
+int umma_split_count(const GemmProblem& p, int num_sms) {
+    return (int)plan_split(kernel_shape(p), num_sms).s;
+}
 
 size_t umma_split_workspace_bytes(const GemmProblem& p, int num_sms) {
-    const SplitPlan pl = plan_split(p, num_sms);
+    const SplitPlan pl = plan_split(kernel_shape(p), num_sms);
     return pl.s > 1 ? pl.partial_bytes : 0;
 }
 
@@ -854,15 +935,18 @@ size_t umma_workspace_bytes(const GemmProblem& p) {
     return (size_t)(2 * ((a * 4 + 255) / 256 * 256) + 2 * ((b * 4 + 255) / 256 * 256));
 }
 
-cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* ws,
+cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status, void* ws,
                              void* split_ws, bool test_stall, cudaStream_t s) {
     UmmaParams prm;
     memset(&prm, 0, sizeof(prm));
     prm.wait_limit_ns = test_stall ? TEST_WAIT_LIMIT_NS : WAIT_LIMIT_NS;
     prm.test_skip_first_load = test_stall ? 1u : 0u;
+    const KernelShape ks = kernel_shape(p_in);
+    const GemmProblem& p = ks.q;                 // the (possibly transposed) problem run
+    prm.c_trans = ks.c_trans ? 1u : 0u;
     const Operand a = operand_a(p), b = operand_b(p);
     const bool is32 = p.dtype == DT_F32;
-    const int BN = is32 ? BN_TF32 : BN_16;
+    const int BN = (int)ks.BN;
     const uint32_t esize = is32 ? 4u : 2u;
     const uint32_t BK = ROW_BYTES / esize, EPB = ROW_BYTES / esize;
 
@@ -934,7 +1018,7 @@ cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, v
     const uint64_t total = (uint64_t)prm.tiles_m * prm.tiles_n * p.batch;
     if (total >= (1ull << 31)) return cudaErrorNotSupported;
     prm.total_tiles = (uint32_t)total;
-    const SplitPlan pl = plan_split(p, num_sms);
+    const SplitPlan pl = plan_split(ks, num_sms);
     if (pl.s > 1 && split_ws) {
         prm.full_tiles = pl.full;
         prm.split_s = pl.s;
@@ -956,9 +1040,16 @@ cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, v
     const int grid = (int)(prm.total_units < (uint32_t)num_sms ? prm.total_units : (uint32_t)num_sms);
     const bool amn = a.mn_major, bmn = b.mn_major;
     cudaError_t e;
+    const bool sm = ks.c_trans;
     switch (p.dtype) {
-        case DT_F16: e = launch_majors<K_F16, BN_16, STAGES_16>(amn, bmn, prm, grid, s); break;
-        case DT_BF16: e = launch_majors<K_BF16, BN_16, STAGES_16>(amn, bmn, prm, grid, s); break;
+        case DT_F16:
+            e = sm ? launch_majors<K_F16, BN_SM, STAGES_SM>(amn, bmn, prm, grid, s)
+                   : launch_majors<K_F16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
+            break;
+        case DT_BF16:
+            e = sm ? launch_majors<K_BF16, BN_SM, STAGES_SM>(amn, bmn, prm, grid, s)
+                   : launch_majors<K_BF16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
+            break;
         case DT_F32:   // planes are K-major whatever op(A), op(B) are
             e = launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32>(prm, grid, s);
             break;
@@ -966,8 +1057,10 @@ cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, v
     }
     if (e != cudaSuccess || prm.split_s <= 1) return e;
     switch (p.dtype) {
-        case DT_F16: return launch_reduce<__half, BN_16>(prm, s);
-        case DT_BF16: return launch_reduce<__nv_bfloat16, BN_16>(prm, s);
+        case DT_F16: return sm ? launch_reduce<__half, BN_SM>(prm, s) : launch_reduce<__half, BN_16>(prm, s);
+        case DT_BF16:
+            return sm ? launch_reduce<__nv_bfloat16, BN_SM>(prm, s)
+                      : launch_reduce<__nv_bfloat16, BN_16>(prm, s);
         default: return launch_reduce<float, BN_TF32>(prm, s);
     }
 }
