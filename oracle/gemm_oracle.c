@@ -31,6 +31,8 @@
  *     what this library's kernels do), or the reference reduce's own encoders
  *     (rounding 1: packHalf2x16 RNE for fp16, truncation to the upper 16 bits
  *     for bf16 -- splitk_reduce_half.comp:5,8, splitk_reduce_m_half.comp:6,9).
+ *   - orc_gemm_rowmajor_f32_splitk: the same segment model for fp32 (the
+ *     decode matvec with K x N weights, matvec_f32_tmpl.comp TB=0).
  *   - f16/bf16 converters: exact RNE (what packHalf2x16 and the GPU's
  *     __float2half_rn do) plus a replica of test/test_h.c:16-41's own
  *     encoders, which the reference's tests use to build their inputs.
@@ -173,6 +175,35 @@ EXPORT void orc_gemm_rowmajor_f32seq(int op_a, int op_b, uint32_t M, uint32_t N,
                 *c = t1 + t2;
             }
     }
+}
+
+/* The fp32 split-K matvec model (matvec_f32_tmpl.comp TB=0 per-output
+ * sequential sums, split into segments and reduced in segment order as
+ * splitk_reduce_f32.comp:61-69 does): K cut into segments of `span`; each
+ * segment a sequential fmaf sum from +0; the segment sums added in order from
+ * +0; then the fp32 epilogue with separate roundings.  span >= K is the
+ * unsplit sequential contract. */
+EXPORT void orc_gemm_rowmajor_f32_splitk(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K,
+                                         uint32_t span, float alpha, const float* A,
+                                         uint32_t lda, const float* B, uint32_t ldb,
+                                         float beta, float* C, uint32_t ldc) {
+    if (span == 0) span = K;
+    for (uint32_t m = 0; m < M; m++)
+        for (uint32_t n = 0; n < N; n++) {
+            float total = 0.0f;
+            for (uint32_t k0 = 0; k0 < K; k0 += span) {
+                uint32_t k1 = k0 + span < K ? k0 + span : K;
+                float part = 0.0f;
+                for (uint32_t k = k0; k < k1; k++)
+                    part = fmaf(A[a_idx(op_a, m, k, lda)], B[b_idx(op_b, k, n, ldb)], part);
+                total += part;
+            }
+            float* c = &C[(size_t)m * ldc + n];
+            float old = beta != 0.0f ? *c : 0.0f;
+            float t1 = alpha * total;
+            float t2 = beta * old;
+            *c = t1 + t2;
+        }
 }
 
 /* Double-precision product of the same contract, written to a separate

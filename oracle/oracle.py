@@ -51,6 +51,8 @@ def _load():
                                        _f, _u16p, _u32, _u32, _i64, _i64, _i64]
     lib.orc_hgemm_rowmajor_splitk.argtypes = [_i, _i, _i, _u32, _u32, _u32, _u32, _f, _u16p, _u32,
                                               _u16p, _u32, _f, _u16p, _u32, _i]
+    lib.orc_gemm_rowmajor_f32_splitk.argtypes = [_i, _i, _u32, _u32, _u32, _u32, _f, _f32p, _u32,
+                                                 _f32p, _u32, _f, _f32p, _u32]
     lib.orc_gen_test_gemm.argtypes = [C.c_uint, _f32p, _sz, _f32p, _sz, _f32p, _sz]
     lib.orc_gen_test_h.argtypes = [C.c_uint, _i, _u16p, _sz, _u16p, _sz, _u16p, _sz, _i]
     lib.orc_sgemm_colmajor_rows_mt.argtypes = [_i, _i, _i, _i, _i, _f, _f32p, _i, _f32p, _i, _f,
@@ -161,6 +163,12 @@ def hgemm_rowmajor_splitk(dtype, op_a, op_b, M, N, K, nseg, alpha, A, lda, B, ld
     (bf16 truncated, splitk_reduce_half.comp:8)."""
     lib.orc_hgemm_rowmajor_splitk(dtype, op_a, op_b, M, N, K, nseg, alpha, A, lda, B, ldb, beta, C, ldc,
                                   rounding)
+
+
+def gemm_rowmajor_f32_splitk(op_a, op_b, M, N, K, span, alpha, A, lda, B, ldb, beta, C, ldc):
+    """fp32 split-K model: segments of `span` k, each a sequential fmaf sum,
+    added in segment order, then the fp32 epilogue (C updated in place)."""
+    lib.orc_gemm_rowmajor_f32_splitk(op_a, op_b, M, N, K, span, alpha, A, lda, B, ldb, beta, C, ldc)
 
 
 # -------------------------------------------------------------- generators

@@ -4,6 +4,7 @@
     python -m vkblas_b200.cases sgemm-simt [--n 4096]                # exact FFMA kernel
     python -m vkblas_b200.cases hgemm  [--n 4096] [--shape M,N,K]    # fp16 tcgen05, hipBLAS T/N
     python -m vkblas_b200.cases gemv   [--m 1] [--splitk 4]          # decode, K=4096, N=14336, M<=64
+    python -m vkblas_b200.cases gemv32 [--m 1] [--trans t|n]         # fp32 decode, K=4096, N=14336
     python -m vkblas_b200.cases batched                              # 256 x 2048^3 fp16 N/N
 
 Inputs are device-resident and seeded; each iteration is one library call on
@@ -22,7 +23,9 @@ from vkblas_b200 import hipblas as hb
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["sgemm", "sgemm-simt", "hgemm", "gemv", "batched"])
+    ap.add_argument("case", choices=["sgemm", "sgemm-simt", "hgemm", "gemv", "gemv32", "batched"])
+    ap.add_argument("--trans", default="t", choices=["t", "n"],
+                    help="gemv32: hipBLAS transA of the weights (t: N x K rows, n: K x N)")
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--shape", default="", help="M,N,K (sgemm, sgemm-simt, hgemm); default n,n,n")
     ap.add_argument("--m", type=int, default=1)
@@ -77,6 +80,24 @@ def main(argv=None) -> int:
                                         Ws[turn[0] % 4].data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
                                         vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F, O,
                                         vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+    elif a.case == "gemv32":
+        K, O, M = 4096, 14336, a.m
+        # four fp32 weight sets (940 MB > 126 MB L2), rotated call by call
+        Ws = [torch.randn(O * K, device="cuda", generator=g) * 0.02 for _ in range(4)]
+        X = torch.randn(M * K, device="cuda", generator=g)
+        C = torch.empty(M * O, device="cuda")
+        if a.splitk:
+            vk.set_splitk(a.splitk)
+        flop, nbytes = 2.0 * M * O * K, 4.0 * (O * K + M * K + M * O)
+        tA = vk.HIPBLAS_OP_T if a.trans == "t" else vk.HIPBLAS_OP_N
+        lda = K if a.trans == "t" else O
+        turn = [0]
+
+        def call():
+            turn[0] += 1
+            return vk.lib.hipblasSgemm(h.h, tA, vk.HIPBLAS_OP_N, O, M, K, al,
+                                       Ws[turn[0] % 4].data_ptr(), lda, X.data_ptr(), K, be,
+                                       C.data_ptr(), O)
     else:
         b, n = 256, 2048
         A = (torch.randn(b * n * n, device="cuda", generator=g) * 0.02).half()

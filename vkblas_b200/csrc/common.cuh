@@ -77,6 +77,10 @@ int gemv_auto_splitk(const GemmProblem& p, int num_sms);
 size_t gemv_workspace_bytes(const GemmProblem& p, int splitk);
 cudaError_t launch_gemv(const GemmProblem& p, int splitk, void* workspace, int* d_status,
                         cudaStream_t s);
+bool gemv_f32_supported(const GemmProblem& p);
+int gemv_f32_auto_splitk(const GemmProblem& p, int num_sms);
+size_t gemv_f32_workspace_bytes(const GemmProblem& p, int splitk);
+cudaError_t launch_gemv_f32(const GemmProblem& p, int splitk, void* workspace, cudaStream_t s);
 bool umma_supported(const GemmProblem& p);
 bool umma_profitable(const GemmProblem& p);
 size_t umma_workspace_bytes(const GemmProblem& p);

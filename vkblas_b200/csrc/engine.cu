@@ -173,6 +173,9 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     int path = 0;
     if ((forced == VKBLAS_PATH_AUTO && cfg.gemv) || forced == VKBLAS_PATH_GEMV) {
         if (gemv_supported(p)) path = VKBLAS_PATH_GEMV;
+        // fp32 decode GEMV, unless the exact FFMA kernel was asked for
+        else if (gemv_f32_supported(p) && (forced == VKBLAS_PATH_GEMV || cfg.sgemm != 1))
+            path = VKBLAS_PATH_GEMV;
     }
     if (!path && (forced == VKBLAS_PATH_AUTO || forced == VKBLAS_PATH_TC)) {
         const int mode = p.dtype == DT_F32 ? cfg.sgemm : cfg.hgemm;   // 0 auto, 1 simt, 2 tc
@@ -184,7 +187,19 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
 
     cudaError_t e = cudaSuccess;
     int splitk = 0, split_used = 1;
-    if (path == VKBLAS_PATH_GEMV) {
+    if (path == VKBLAS_PATH_GEMV && p.dtype == DT_F32) {
+        splitk = tls.splitk > 0 ? tls.splitk : cfg.gemv_splitk > 0 ? cfg.gemv_splitk
+                                                                   : gemv_f32_auto_splitk(p, ds->num_sms);
+        if (splitk > 64) splitk = 64;
+        void* ws = nullptr;
+        const size_t need = gemv_f32_workspace_bytes(p, splitk);
+        if (need) {
+            ws = workspace(ds, 0, s, need);
+            if (!ws) splitk = 1;
+        }
+        e = launch_gemv_f32(p, splitk, ws, s);
+        split_used = splitk;
+    } else if (path == VKBLAS_PATH_GEMV) {
         splitk = tls.splitk > 0 ? tls.splitk : cfg.gemv_splitk > 0 ? cfg.gemv_splitk
                                                                    : gemv_auto_splitk(p, ds->num_sms);
         if (splitk > 16) splitk = 16;
