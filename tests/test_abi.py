@@ -26,10 +26,14 @@ import vkblas_b200 as vk  # noqa: E402
 from vkblas_b200 import hipblas as hb  # noqa: E402
 
 
-def _declared_functions():
+def _declared_functions(headers=None):
     names = set()
     for f in os.listdir(INCLUDE):
         if not f.endswith(".h"):
+            continue
+        if headers is None and f == "vkblas_cublas.h":    # declares libvkblas_cublas.so's API
+            continue
+        if headers is not None and f not in headers:
             continue
         text = open(os.path.join(INCLUDE, f)).read()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)

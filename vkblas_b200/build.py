@@ -26,6 +26,11 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libvkblas_hipblas.so")
+# cuBLAS GEMM interposer for LD_PRELOAD into CUDA applications: the same engine
+# objects plus cublas_shim.cpp, exporting only cublas* (under the real
+# library's version name, which is what applications bind) and its counter.
+CUBLAS_LIB = os.path.join(PKG, "libvkblas_cublas.so")
+CUBLAS_SHIM = "cublas_shim"
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -39,6 +44,18 @@ VERSION_SCRIPT = """{
     vkblas_*;
     hipblas*;
     rocblas_*;
+  local:
+    *;
+};
+"""
+
+CUBLAS_VERSION_SCRIPT = """libcublas.so.12 {
+  global:
+    cublas*;
+};
+VKBLAS_CUBLAS_1 {
+  global:
+    vkblas_cublas_calls;
   local:
     *;
 };
@@ -90,14 +107,24 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
         for out in ex.map(_run, jobs):
             if out.strip():
                 log.append(out)
-    if jobs or not os.path.exists(LIB) or _stale(LIB, objs):
-        vs = os.path.join(BUILD, "exports.map")
+    shim = os.path.join(BUILD, CUBLAS_SHIM + ".o")
+    hip_objs = [o for o in objs if o != shim]
+    cub_objs = [o for o in objs if not o.endswith("hipblas_shim.o")]
+    for lib, lib_objs, script, name in ((LIB, hip_objs, VERSION_SCRIPT, "exports.map"),
+                                        (CUBLAS_LIB, cub_objs, CUBLAS_VERSION_SCRIPT,
+                                         "exports_cublas.map")):
+        if not (jobs or not os.path.exists(lib) or _stale(lib, lib_objs)):
+            continue
+        vs = os.path.join(BUILD, name)
         with open(vs, "w") as fh:
-            fh.write(VERSION_SCRIPT)
-        tmp = LIB + ".tmp"
-        _run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static",
-              "-Xlinker", "--version-script=" + vs, "-ldl", "-lpthread", "-lrt"])
-        os.replace(tmp, LIB)
+            fh.write(script)
+        tmp = lib + ".tmp"
+        # -Bsymbolic-functions: the library's own calls (the shims into the
+        # engine) bind inside it, whatever else the process has loaded.
+        _run([NVCC, *ARCH, "-shared", "-o", tmp, *lib_objs, "-cudart", "static",
+              "-Xlinker", "--version-script=" + vs, "-Xlinker", "-Bsymbolic-functions",
+              "-ldl", "-lpthread", "-lrt"])
+        os.replace(tmp, lib)
     text = "\n".join(log)
     if verbose and text:
         print(text)
