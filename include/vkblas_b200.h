@@ -72,6 +72,9 @@ int vkblas_b200_last_path(void);
  * path the number of K ranges the tiles of its last, partial wave were cut
  * into (their partial sums are added by a second kernel); 1 = no split. */
 int vkblas_b200_last_split(void);
+/* 1 when that call ran on 2-CTA clusters (tcgen05 cta_group::2, 256-row
+ * tiles: each CTA loads half of the B tile), else 0. */
+int vkblas_b200_last_pair(void);
 /* Thread-local split-K factor for the GEMV path: 0 = automatic, else 1..16. */
 void vkblas_b200_set_splitk(int splitk);
 

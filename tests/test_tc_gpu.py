@@ -32,7 +32,8 @@ def _mk(dtype, rng, n):
     return orc.widen(1 if dtype == vk.DT_BF16 else 0, bits), bits
 
 
-def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8, split=None):
+def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8, split=None,
+         pair=None):
     import torch
     rng = np.random.default_rng(M * 7 + N * 3 + K + op_a * 2 + op_b + dtype * 11 + batch)
     lda = (M if op_a else K)
@@ -72,6 +73,8 @@ def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8
     assert vk.last_path() == vk.PATH_TC
     if split is not None:
         assert (vk.last_split() > 1) == split, f"K-split count {vk.last_split()}"
+    if pair is not None:
+        assert vk.last_pair() == pair, f"CTA pair mode {vk.last_pair()}"
     check_status()
     got = host(dC) if dtype == vk.DT_F32 else orc.widen(dt16, host_u16(dC))
     want = orc.gemm_rowmajor_f64(op_a, op_b, M, N, K, alpha, np.ascontiguousarray(Af), lda,
@@ -200,3 +203,27 @@ def test_tc_small_m_transposed(dtype, ops, case, cuda):
 
 def test_tc_small_m_batched_broadcast(cuda):
     _run(vk.DT_F16, 0, 1, 12, 640, 256, 1.0, 0.5, batch=3, bcast="b", split=False)
+
+
+# 256-row tiles on 2-CTA clusters (tcgen05 cta_group::2: each CTA loads its
+# 128 rows of A and half of the B tile) whenever M >= 256 and no K split is
+# planned.  (shape, pair)
+PAIR_SHAPES = [
+    ((512, 512, 256), True),
+    ((300, 520, 200), True),        # second pair tile: the other CTA has 44 rows
+    ((384, 264, 200), True),        # the other CTA's rows entirely past M in tile 2
+    ((1024, 768, 512), True),
+    ((200, 300, 136), False),
+]
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_BF16, vk.DT_F32], ids=["f16", "bf16", "f32"])
+@pytest.mark.parametrize("ops", [(0, 0), (0, 1), (1, 0), (1, 1)], ids=["NN", "NT", "TN", "TT"])
+@pytest.mark.parametrize("case", PAIR_SHAPES, ids=[f"{m}x{n}x{k}" for (m, n, k), _ in PAIR_SHAPES])
+def test_tc_cta_pair_tiles(dtype, ops, case, cuda):
+    (M, N, K), pair = case
+    _run(dtype, ops[0], ops[1], M, N, K, 0.5, 0.25, pair=pair)
+
+
+def test_tc_split_shapes_stay_single_cta(cuda):
+    _run(vk.DT_F16, 0, 1, 256, 256, 4096, 1.0, 0.0, split=True, pair=False)

@@ -61,6 +61,7 @@ def _load() -> C.CDLL:
     lib.vkblas_b200_get_path.restype = i32
     lib.vkblas_b200_last_path.restype = i32
     lib.vkblas_b200_last_split.restype = i32
+    lib.vkblas_b200_last_pair.restype = i32
     lib.vkblas_b200_set_splitk.argtypes = [i32]
     lib.vkblas_b200_set_test_stall.argtypes = [i32]
     lib.vkblas_b200_device_status.argtypes = [i32]
@@ -113,6 +114,11 @@ def last_path() -> int:
 def last_split() -> int:
     """K-split count of this thread's last call (1 = none)."""
     return _get().vkblas_b200_last_split()
+
+
+def last_pair() -> bool:
+    """Whether this thread's last call ran on 2-CTA clusters (256-row tiles)."""
+    return bool(_get().vkblas_b200_last_pair())
 
 
 def set_splitk(s: int) -> None:

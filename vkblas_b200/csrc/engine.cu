@@ -18,6 +18,7 @@
 // Environment overrides, read once: VKBLAS_SGEMM=ffma|3xtf32|auto,
 // VKBLAS_HGEMM=simt|tc|auto, VKBLAS_GEMV=0|1, VKBLAS_GEMV_SPLITK=n,
 // VKBLAS_TC_SPLIT=0|1 (K-split of the tensor-core GEMM's last wave),
+// VKBLAS_TC_PAIR=0|1 (256-row tiles on 2-CTA clusters; read in umma_gemm.cu),
 // VKBLAS_TRACE=1 (one line per call on stderr).
 #include <atomic>
 #include <cstdio>
@@ -137,6 +138,7 @@ struct ThreadState {
     int splitk = 0;
     int last = VKBLAS_PATH_AUTO;
     int last_split = 1;
+    int last_pair = 0;
     int test_stall = 0;
 };
 thread_local ThreadState tls;
@@ -186,7 +188,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     if (!path) return VKBLAS_ERR_FALLBACK;
 
     cudaError_t e = cudaSuccess;
-    int splitk = 0, split_used = 1;
+    int splitk = 0, split_used = 1, pair_used = 0;
     if (path == VKBLAS_PATH_GEMV && p.dtype == DT_F32) {
         splitk = tls.splitk > 0 ? tls.splitk : cfg.gemv_splitk > 0 ? cfg.gemv_splitk
                                                                    : gemv_f32_auto_splitk(p, ds->num_sms);
@@ -229,10 +231,13 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
                           : launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, wsplit,
                                              tls.test_stall != 0, s);
         split_used = wsplit ? umma_split_count(p, ds->num_sms) : 1;
+        pair_used = umma_uses_pair(p, ds->num_sms, wsplit != nullptr) ? 1 : 0;
+        if (pair_used) split_used = 1;
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
             cudaGetLastError();
             path = VKBLAS_PATH_SIMT;       // operands TMA cannot describe: exact SIMT path
             split_used = 1;
+            pair_used = 0;
             e = launch_simt_gemm(p, s);
         } else if (e == cudaErrorNotSupported) {
             cudaGetLastError();
@@ -253,6 +258,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     }
     tls.last = path;
     tls.last_split = split_used;
+    tls.last_pair = pair_used;
     return VKBLAS_OK;
 }
 
@@ -371,6 +377,7 @@ VKB_EXPORT void vkblas_b200_set_path(int path) {
 VKB_EXPORT int vkblas_b200_get_path(void) { return tls.path; }
 VKB_EXPORT int vkblas_b200_last_path(void) { return tls.last; }
 VKB_EXPORT int vkblas_b200_last_split(void) { return tls.last_split; }
+VKB_EXPORT int vkblas_b200_last_pair(void) { return tls.last_pair; }
 VKB_EXPORT void vkblas_b200_set_splitk(int splitk) {
     tls.splitk = splitk < 0 ? 0 : splitk > 16 ? 16 : splitk;
 }

@@ -181,7 +181,7 @@ __device__ __forceinline__ void store_col32(T* cb, uint32_t row, uint32_t n0, ui
     }
 }
 
-template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES>
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
 struct Cfg {
     static constexpr int E = (KIND == K_TF32X3) ? 4 : 2;
     static constexpr int PLANES = (KIND == K_TF32X3) ? 2 : 1;
@@ -189,8 +189,12 @@ struct Cfg {
     static constexpr int UK = 32 / E;                 // K per UMMA instruction (16 or 8)
     static constexpr int KSTEPS = BK / UK;            // 4
     static constexpr int EPB = ROW_BYTES / E;         // elements per 128-byte MN slab
+    // A CTA pair (PAIR) computes 256 x BN tiles: each CTA loads its 128 rows of
+    // A and BN/2 columns of B.
+    static constexpr int BM_TILE = PAIR ? 2 * BM : BM;
+    static constexpr int BNC = PAIR ? BN / 2 : BN;             // B rows (N) per CTA
     static constexpr uint32_t A_PLANE = BM * ROW_BYTES;
-    static constexpr uint32_t B_PLANE = BN * ROW_BYTES;
+    static constexpr uint32_t B_PLANE = BNC * ROW_BYTES;
     static constexpr uint32_t STAGE_BYTES = PLANES * (A_PLANE + B_PLANE);
     // The tensor core's fp32 accumulation truncates, so its error grows
     // linearly with the number of accumulating MMAs (measured on B200: relative
@@ -209,16 +213,19 @@ struct Cfg {
     static constexpr uint32_t TMEM_COLS = NBUF * BN;                // 512
     static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
     static constexpr uint32_t IDESC =
-        instr_desc(KIND == K_F16 ? 0u : KIND == K_BF16 ? 1u : 2u, A_MN, B_MN, BM, BN);
+        instr_desc(KIND == K_F16 ? 0u : KIND == K_BF16 ? 1u : 2u, A_MN, B_MN, BM_TILE, BN);
+    // Accumulator hand-back: every epilogue thread of the CTA (of both CTAs
+    // for a pair, on the even CTA's barrier).
+    static constexpr uint32_t TEMPTY_COUNT = (PAIR ? 2u : 1u) * 32u * EPI_WARPS;
     static constexpr uint32_t SLAB = BK * ROW_BYTES;  // MN-major: one 128-byte-wide slab
     static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
     static_assert(SEG_KB == 0 || EPI_COLS <= 64, "segmented epilogue keeps EPI_COLS fp32 sums per thread");
 };
 
-template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES>
-__global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
+__global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREADS, 1)
     umma_gemm_kernel(const __grid_constant__ UmmaParams p) {
-    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES>;
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
     using TOut = typename OutT<KIND>::T;
     constexpr uint32_t NBUF = C_::NBUF;
 
@@ -239,6 +246,14 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // CTA pairs: rank 0 issues the MMAs; both CTAs' copies complete on its full
+    // barriers and both CTAs' epilogues hand accumulators back on its tempty
+    // barriers.  Work units are per pair.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool issuer = rank == 0;
+    const uint32_t unit0 = PAIR ? blockIdx.x >> 1 : blockIdx.x;
+    const uint32_t ustride = PAIR ? gridDim.x >> 1 : gridDim.x;
+    auto to_issuer = [&](uint32_t bar) { return PAIR ? mapa_shared(bar, 0) : bar; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -247,7 +262,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
         }
         for (uint32_t a = 0; a < NBUF; a++) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 32 * C_::EPI_WARPS);
+            mbar_init(tempty_bar(a), C_::TEMPTY_COUNT);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -263,10 +278,16 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
         }
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), C_::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(smem_u32(tmem_slot), C_::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), C_::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();      // the peer's barriers are initialised
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     // Let a programmatically dependent split_reduce_kernel get resident; it
@@ -279,11 +300,12 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_parity = 0;   // per stage: issued ever / last parity
             bool ok = true;
-            for (uint32_t u = blockIdx.x; ok && u < p.total_units; u += gridDim.x) {
+            for (uint32_t u = unit0; ok && u < p.total_units; u += ustride) {
                 uint32_t t, sp, ukb0, ukb1, b, mb, nb;
                 unit_info(p, u, t, sp, ukb0, ukb1);
                 tile_coords(p, t, b, mb, nb);
-                const int32_t m0 = (int32_t)(mb * BM), n0 = (int32_t)(nb * BN);
+                const int32_t m0 = (int32_t)(mb * C_::BM_TILE + rank * BM);
+                const int32_t n0 = (int32_t)(nb * BN + rank * C_::BNC);
                 const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
                 for (uint32_t kb = ukb0; kb < ukb1; kb++) {
                     if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
@@ -291,8 +313,8 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                         ok = false;
                         break;
                     }
-                    const uint32_t fb = full_bar(stage);
-                    if (p.test_skip_first_load && u == blockIdx.x && kb == ukb0) {
+                    const uint32_t fb = to_issuer(full_bar(stage));
+                    if (p.test_skip_first_load && u == unit0 && kb == ukb0) {
                         // Test hook: leave this stage empty so its consumer's
                         // bounded wait runs out (no copy is issued).
                         if (++stage == STAGES) {
@@ -301,27 +323,33 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                         }
                         continue;
                     }
-                    mbar_arrive_expect_tx(fb, C_::STAGE_BYTES);
+                    // The issuer expects both CTAs' bytes of a pair stage.
+                    if (issuer) mbar_arrive_expect_tx(full_bar(stage), (PAIR ? 2u : 1u) * C_::STAGE_BYTES);
                     const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
                     const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
                     const int32_t k0 = (int32_t)(kb * C_::BK);
+                    auto load = [&](uint32_t dst, const CUtensorMap* m, int32_t c0, int32_t c1,
+                                    int32_t c2) {
+                        if constexpr (PAIR) tma_load_3d_pair(dst, m, fb, c0, c1, c2);
+                        else tma_load_3d(dst, m, fb, c0, c1, c2);
+                    };
 #pragma unroll
                     for (int pl = 0; pl < C_::PLANES; pl++) {
                         if (!A_MN) {
-                            tma_load_3d(sA + pl * C_::A_PLANE, &p.tmA[pl], fb, k0, m0, ba);
+                            load(sA + pl * C_::A_PLANE, &p.tmA[pl], k0, m0, ba);
                         } else {
 #pragma unroll
                             for (int j = 0; j < BM / C_::EPB; j++)
-                                tma_load_3d(sA + pl * C_::A_PLANE + j * C_::SLAB, &p.tmA[pl], fb,
-                                            m0 + j * C_::EPB, k0, ba);
+                                load(sA + pl * C_::A_PLANE + j * C_::SLAB, &p.tmA[pl],
+                                     m0 + j * C_::EPB, k0, ba);
                         }
                         if (!B_MN) {
-                            tma_load_3d(sB + pl * C_::B_PLANE, &p.tmB[pl], fb, k0, n0, bb);
+                            load(sB + pl * C_::B_PLANE, &p.tmB[pl], k0, n0, bb);
                         } else {
 #pragma unroll
-                            for (int j = 0; j < BN / C_::EPB; j++)
-                                tma_load_3d(sB + pl * C_::B_PLANE + j * C_::SLAB, &p.tmB[pl], fb,
-                                            n0 + j * C_::EPB, k0, bb);
+                            for (int j = 0; j < C_::BNC / C_::EPB; j++)
+                                load(sB + pl * C_::B_PLANE + j * C_::SLAB, &p.tmB[pl],
+                                     n0 + j * C_::EPB, k0, bb);
                         }
                     }
                     issued_mask |= 1u << stage;
@@ -332,18 +360,20 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                     }
                 }
             }
-            // Never leave with copies in flight: wait for the last fill of every stage.
+            // Never leave with copies in flight: wait for the last fill of every
+            // stage (the issuer's full barrier; in the other CTA of a pair, the
+            // stage's release by the issuer's MMAs, which follows its landing).
             for (int s = 0; s < STAGES; s++)
                 if (issued_mask & (1u << s))
-                    drain_bar_wait(full_bar(s), (issued_parity >> s) & 1u, p.status,
-                                   DS_TIMEOUT_PRODUCER, DRAIN_LIMIT_NS);
+                    drain_bar_wait(issuer ? full_bar(s) : empty_bar(s), (issued_parity >> s) & 1u,
+                                   p.status, DS_TIMEOUT_PRODUCER, DRAIN_LIMIT_NS);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
-        if (lane == 0) {
+        if (lane == 0 && issuer) {
             uint32_t stage = 0, phase = 0, u = 0;          // u: accumulator hand-overs so far
             bool ok = true;
-            for (uint32_t w = blockIdx.x; ok && w < p.total_units; w += gridDim.x) {
+            for (uint32_t w = unit0; ok && w < p.total_units; w += ustride) {
                 uint32_t t, sp, ukb0, ukb1;
                 unit_info(p, w, t, sp, ukb0, ukb1);
                 const uint32_t seg_kb = C_::SEG_KB ? C_::SEG_KB : (ukb1 - ukb0);
@@ -382,25 +412,35 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                             }
                             const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
                             if constexpr (KIND == K_TF32X3) {
-                                mma_tf32(d, ad[1], bd[0], C_::IDESC, first);   // A_small * B_big
-                                mma_tf32(d, ad[0], bd[1], C_::IDESC, 1u);      // A_big * B_small
-                                mma_tf32(d, ad[0], bd[0], C_::IDESC, 1u);      // A_big * B_big
+                                if constexpr (PAIR) {
+                                    mma_tf32_pair(d, ad[1], bd[0], C_::IDESC, first);
+                                    mma_tf32_pair(d, ad[0], bd[1], C_::IDESC, 1u);
+                                    mma_tf32_pair(d, ad[0], bd[0], C_::IDESC, 1u);
+                                } else {
+                                    mma_tf32(d, ad[1], bd[0], C_::IDESC, first);   // A_small * B_big
+                                    mma_tf32(d, ad[0], bd[1], C_::IDESC, 1u);      // A_big * B_small
+                                    mma_tf32(d, ad[0], bd[0], C_::IDESC, 1u);      // A_big * B_big
+                                }
                             } else {
-                                mma_f16(d, ad[0], bd[0], C_::IDESC, first);
+                                if constexpr (PAIR) mma_f16_pair(d, ad[0], bd[0], C_::IDESC, first);
+                                else mma_f16(d, ad[0], bd[0], C_::IDESC, first);
                             }
                         }
-                        tc_commit(empty_bar(stage));
+                        if constexpr (PAIR) tc_commit_pair_mc(empty_bar(stage), 0x3);   // both CTAs' stage
+                        else tc_commit(empty_bar(stage));
                         if (++stage == STAGES) {
                             stage = 0;
                             phase ^= 1u;
                         }
                     }
                     if (!ok) break;
-                    tc_commit(tfull_bar(buf));
+                    if constexpr (PAIR) tc_commit_pair_mc(tfull_bar(buf), 0x3);    // both epilogues
+                    else tc_commit(tfull_bar(buf));
                 }
             }
             // Never leave with MMAs in flight.
-            tc_commit(drain_bar);
+            if constexpr (PAIR) tc_commit_pair(drain_bar);
+            else tc_commit(drain_bar);
             drain_bar_wait(drain_bar, 0, p.status, DS_TIMEOUT_MMA, DRAIN_LIMIT_NS);
         }
     } else {
@@ -424,11 +464,16 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 32; i++) __stcg(P + i * BM, v[i]);
         };
-        for (uint32_t w = blockIdx.x; ok && w < p.total_units; w += gridDim.x) {
+        // Hand an accumulator buffer back to the MMA issuer.
+        auto release = [&](uint32_t buf) {
+            if constexpr (PAIR) mbar_arrive_cluster(to_issuer(tempty_bar(buf)));
+            else mbar_arrive(tempty_bar(buf));
+        };
+        for (uint32_t w = unit0; ok && w < p.total_units; w += ustride) {
             uint32_t t, sp, ukb0, ukb1, b, mb, nb;
             unit_info(p, w, t, sp, ukb0, ukb1);
             tile_coords(p, t, b, mb, nb);
-            const uint32_t m = mb * BM + row;
+            const uint32_t m = mb * C_::BM_TILE + rank * BM + row;
             TOut* cb = Cbase + p.sc * (int64_t)b;
             TOut* crow = cb + (size_t)m * p.ldc;
             if constexpr (C_::SEG_KB == 0) {
@@ -458,7 +503,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(tempty_bar(buf));
+                release(buf);
                 u++;
             } else {
                 float sum[C_::EPI_COLS / 32][32];
@@ -481,7 +526,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
                                            : __uint_as_float(r[i]);
                     }
                     tc_fence_before();
-                    mbar_arrive(tempty_bar(buf));
+                    release(buf);
                 }
                 if (!ok) break;
 #pragma unroll
@@ -505,9 +550,13 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES>::THREADS, 1)
     }
 
     __syncthreads();
+    // A pair leaves together: the issuer's last commits arrive on the other
+    // CTA's barriers, and its MMAs read the other CTA's shared memory.
+    if constexpr (PAIR) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C_::TMEM_COLS);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C_::TMEM_COLS);
+        else tmem_dealloc(tmem_base, C_::TMEM_COLS);
     }
 }
 
@@ -761,11 +810,14 @@ uint64_t plane_rows(const Operand& o) { return o.mn_major ? o.inner : o.outer; }
 uint32_t plane_k(const Operand& o) { return (uint32_t)(o.mn_major ? o.outer : o.inner); }
 uint64_t plane_elems(const Operand& o) { return o.nb * plane_rows(o) * rup4(plane_k(o)); }
 
-template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES>
-cudaError_t launch_kind(const UmmaParams& prm, int grid, cudaStream_t s) {
-    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES>;
-    auto kern = umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES>;
+// One CTA per SM (persistent over `units` work units), or for PAIR one 2-CTA
+// cluster per pair of SMs, as many clusters as the device can hold at once.
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
+cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cudaStream_t s) {
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
+    auto kern = umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
     static std::atomic<uint64_t> attr_done{0};     // one bit per device
+    static int max_clusters[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
@@ -773,19 +825,56 @@ cudaError_t launch_kind(const UmmaParams& prm, int grid, cudaStream_t s) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)C_::SMEM_BYTES);
         if (e != cudaSuccess) return e;
+        if (PAIR) {
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3((uint32_t)(num_sms & ~1));
+            q.blockDim = dim3(C_::THREADS);
+            q.dynamicSmemBytes = C_::SMEM_BYTES;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+            q.attrs = at;
+            q.numAttrs = 1;
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, kern, &q);
+            if (e != cudaSuccess || n < 1) {
+                cudaGetLastError();
+                return cudaErrorNotSupported;
+            }
+            max_clusters[dev & 63] = n;
+        }
         attr_done.fetch_or(bit);
     }
-    kern<<<grid, C_::THREADS, C_::SMEM_BYTES, s>>>(prm);
+    if (!PAIR) {
+        const uint32_t grid = units < (uint32_t)num_sms ? units : (uint32_t)num_sms;
+        kern<<<grid, C_::THREADS, C_::SMEM_BYTES, s>>>(prm);
+        count_launch();
+        return cudaGetLastError();
+    }
+    const uint32_t mc = (uint32_t)max_clusters[dev & 63];
+    const uint32_t clusters = units < mc ? units : mc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(C_::THREADS);
+    cfg.dynamicSmemBytes = C_::SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
-template <int KIND, int BN, int STAGES>
-cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, int grid, cudaStream_t s) {
-    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES>(prm, grid, s);
-    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES>(prm, grid, s);
-    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES>(prm, grid, s);
-    return launch_kind<KIND, true, true, BN, STAGES>(prm, grid, s);
+template <int KIND, int BN, int STAGES, bool PAIR>
+cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, uint32_t units, int num_sms,
+                          cudaStream_t s) {
+    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES, PAIR>(prm, units, num_sms, s);
+    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES, PAIR>(prm, units, num_sms, s);
+    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES, PAIR>(prm, units, num_sms, s);
+    return launch_kind<KIND, true, true, BN, STAGES, PAIR>(prm, units, num_sms, s);
 }
 
 // The reduce of split tiles, launched so that it may become resident while
@@ -809,6 +898,17 @@ cudaError_t launch_reduce(const UmmaParams& prm, cudaStream_t s) {
 }
 
 constexpr int BN_16 = 256, STAGES_16 = 4;
+// CTA pairs (256-row tiles): half of B per CTA leaves room for deeper rings.
+constexpr int STAGES_16P = 6, STAGES_TF32P = 4;
+
+// VKBLAS_TC_PAIR=0 keeps every tensor-core GEMM on single-CTA tiles.
+bool pair_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("VKBLAS_TC_PAIR");
+        return !(e && *e && atoi(e) == 0);
+    }();
+    return on;
+}
 // Small-M 2-byte GEMMs (decode with up to 64 tokens) run transposed: weight
 // rows on the MMA's 128 lanes, tokens on a 64-wide N tile, an 8-deep ring.
 constexpr int BN_SM = 64, STAGES_SM = 8;
@@ -919,6 +1019,12 @@ bool umma_profitable(const GemmProblem& p) {
     return (p.M >= 32 && p.N >= 32) || small_m_swap(p);
 }
 
+bool umma_uses_pair(const GemmProblem& p, int num_sms, bool split_ws) {
+    const KernelShape ks = kernel_shape(p);
+    const SplitPlan pl = plan_split(ks, num_sms);
+    return pair_enabled() && !ks.c_trans && !(pl.s > 1 && split_ws) && ks.q.M >= 2u * BM;
+}
+
 int umma_split_count(const GemmProblem& p, int num_sms) {
     return (int)plan_split(kernel_shape(p), num_sms).s;
 }
@@ -949,6 +1055,10 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     const int BN = (int)ks.BN;
     const uint32_t esize = is32 ? 4u : 2u;
     const uint32_t BK = ROW_BYTES / esize, EPB = ROW_BYTES / esize;
+    // 256-row tiles on CTA pairs when no split is planned and M fills them.
+    const SplitPlan pl = plan_split(ks, num_sms);
+    const bool pair = umma_uses_pair(p_in, num_sms, split_ws != nullptr);
+    const uint32_t bn_cta = pair ? (uint32_t)BN / 2 : (uint32_t)BN;      // B rows per CTA
 
     auto box_for = [&](const Operand& o, uint32_t tile_rows, uint32_t& bi, uint32_t& bo) {
         if (o.mn_major) { bi = EPB; bo = BK; }          // 128-byte MN slab x BK k-rows
@@ -956,7 +1066,7 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     };
     uint32_t abi, abo, bbi, bbo;
     box_for(a, BM, abi, abo);
-    box_for(b, (uint32_t)BN, bbi, bbo);
+    box_for(b, bn_cta, bbi, bbo);
 
     if (!is32) {
         const CUtensorMapDataType dt =
@@ -982,8 +1092,8 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
         // K-major boxes: BK (32 fp32 = 128 bytes) x tile rows
         if (!make_tmap(&prm.tmA[0], dt, 4, a_big, plane_k(a), ar, lda_o, a.nb, sa_o, BK, BM) ||
             !make_tmap(&prm.tmA[1], dt, 4, a_small, plane_k(a), ar, lda_o, a.nb, sa_o, BK, BM) ||
-            !make_tmap(&prm.tmB[0], dt, 4, b_big, plane_k(b), br, ldb_o, b.nb, sb_o, BK, BN) ||
-            !make_tmap(&prm.tmB[1], dt, 4, b_small, plane_k(b), br, ldb_o, b.nb, sb_o, BK, BN))
+            !make_tmap(&prm.tmB[0], dt, 4, b_big, plane_k(b), br, ldb_o, b.nb, sb_o, BK, bn_cta) ||
+            !make_tmap(&prm.tmB[1], dt, 4, b_small, plane_k(b), br, ldb_o, b.nb, sb_o, BK, bn_cta))
             return cudaErrorNotSupported;
         auto split = [&](const Operand& o, uint32_t ldo, float* big, float* small) {
             if (!o.mn_major) {
@@ -1012,14 +1122,14 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     prm.ldc = p.ldc;
     prm.sc = p.sc;
     prm.M = p.M; prm.N = p.N; prm.K = p.K; prm.batch = p.batch;
-    prm.tiles_m = (p.M + BM - 1) / BM;
+    const uint32_t bm_tile = pair ? 2u * BM : (uint32_t)BM;
+    prm.tiles_m = (p.M + bm_tile - 1) / bm_tile;
     prm.tiles_n = (p.N + BN - 1) / BN;
     prm.num_kb = (p.K + BK - 1) / BK;
     const uint64_t total = (uint64_t)prm.tiles_m * prm.tiles_n * p.batch;
     if (total >= (1ull << 31)) return cudaErrorNotSupported;
     prm.total_tiles = (uint32_t)total;
-    const SplitPlan pl = plan_split(ks, num_sms);
-    if (pl.s > 1 && split_ws) {
+    if (!pair && pl.s > 1 && split_ws) {
         prm.full_tiles = pl.full;
         prm.split_s = pl.s;
         prm.split_kb = pl.kb_per;
@@ -1037,21 +1147,24 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     prm.status = d_status;
     prm.c_vec_ok = al16(p.C) && ((uint64_t)p.ldc * esize) % 16 == 0 &&
                    (p.batch == 1 || ((uint64_t)p.sc * esize) % 16 == 0);
-    const int grid = (int)(prm.total_units < (uint32_t)num_sms ? prm.total_units : (uint32_t)num_sms);
+    const uint32_t units = prm.total_units;
     const bool amn = a.mn_major, bmn = b.mn_major;
     cudaError_t e;
     const bool sm = ks.c_trans;
     switch (p.dtype) {
         case DT_F16:
-            e = sm ? launch_majors<K_F16, BN_SM, STAGES_SM>(amn, bmn, prm, grid, s)
-                   : launch_majors<K_F16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
+            e = sm     ? launch_majors<K_F16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s)
+                : pair ? launch_majors<K_F16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
+                       : launch_majors<K_F16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_BF16:
-            e = sm ? launch_majors<K_BF16, BN_SM, STAGES_SM>(amn, bmn, prm, grid, s)
-                   : launch_majors<K_BF16, BN_16, STAGES_16>(amn, bmn, prm, grid, s);
+            e = sm     ? launch_majors<K_BF16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s)
+                : pair ? launch_majors<K_BF16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
+                       : launch_majors<K_BF16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_F32:   // planes are K-major whatever op(A), op(B) are
-            e = launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32>(prm, grid, s);
+            e = pair ? launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32P, true>(prm, units, num_sms, s)
+                     : launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32, false>(prm, units, num_sms, s);
             break;
         default: return cudaErrorInvalidValue;
     }
