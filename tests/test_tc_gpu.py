@@ -225,5 +225,15 @@ def test_tc_cta_pair_tiles(dtype, ops, case, cuda):
     _run(dtype, ops[0], ops[1], M, N, K, 0.5, 0.25, pair=pair)
 
 
-def test_tc_split_shapes_stay_single_cta(cuda):
-    _run(vk.DT_F16, 0, 1, 256, 256, 4096, 1.0, 0.0, split=True, pair=False)
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_F32], ids=["f16", "f32"])
+def test_tc_pair_tiles_with_split(dtype, cuda):
+    """A pair tile split along K: each CTA publishes its 128-row half of the
+    partial tile and the reduce kernel adds them per half."""
+    _run(dtype, 0, 1, 256, 256, 4096, 1.0, 0.5, split=True, pair=True)
+
+
+@pytest.mark.parametrize("dtype", [vk.DT_F16, vk.DT_F32], ids=["f16", "f32"])
+def test_tc_pair_wave_tail_split(dtype, cuda):
+    """75 pair tiles (one per batch entry) on 74 SM pairs: whole waves run
+    unsplit, only the last pair tile is split along K."""
+    _run(dtype, 0, 0, 256, 40, 4096, 1.0, 0.0, batch=75, split=True, pair=True)

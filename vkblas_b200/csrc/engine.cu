@@ -232,7 +232,6 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
                                              tls.test_stall != 0, s);
         split_used = wsplit ? umma_split_count(p, ds->num_sms) : 1;
         pair_used = umma_uses_pair(p, ds->num_sms, wsplit != nullptr) ? 1 : 0;
-        if (pair_used) split_used = 1;
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
             cudaGetLastError();
             path = VKBLAS_PATH_SIMT;       // operands TMA cannot describe: exact SIMT path

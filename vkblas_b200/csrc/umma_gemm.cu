@@ -458,9 +458,11 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
         // split_reduce_kernel adds the splits in order and writes C.  Partial
         // tiles are stored column by column ([BN][BM], row fastest): lane =
         // row, so for each column a warp writes one contiguous 128-byte line.
+        // Layout [split tile][split][half][BN][BM]: a pair tile has two
+        // 128-row halves, one per CTA.
         auto split_publish = [&](uint32_t t, uint32_t sp, const float (&v)[32], int c) {
-            float* P = p.partial + ((size_t)(t - p.full_tiles) * p.split_s + sp) * BM * BN +
-                       (size_t)(col0 + c * 32) * BM + row;
+            const size_t half = ((size_t)(t - p.full_tiles) * p.split_s + sp) * (PAIR ? 2u : 1u) + rank;
+            float* P = p.partial + half * BM * BN + (size_t)(col0 + c * 32) * BM + row;
 #pragma unroll
             for (int i = 0; i < 32; i++) __stcg(P + i * BM, v[i]);
         };
@@ -566,11 +568,12 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
 // round trips), the chunk is transposed through shared memory and written along C's
 // rows.  Launched as a programmatic dependent of the GEMM grid that wrote the
 // partials.
-template <typename TOut, int BN>
+template <typename TOut, int BN, int TILE_ROWS>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant__ UmmaParams p) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     constexpr uint32_t RC = 32, CC = 64;                // chunk rows x columns
-    constexpr uint32_t CM = BM / RC, CN = BN / CC;
+    constexpr uint32_t CM = TILE_ROWS / RC, CN = BN / CC;
+    constexpr uint32_t H = TILE_ROWS / BM;              // 128-row halves per tile
     __shared__ float tile[CC][RC + 1];                  // [column][row]
     const uint32_t st = blockIdx.x / (CM * CN);          // split tile
     const uint32_t r = blockIdx.x - st * (CM * CN);
@@ -580,8 +583,10 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
     float alpha = p.alpha, beta = p.beta;
     load_scalars(p.d_alpha, p.d_beta, alpha, beta);
     const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const float* P = p.partial + (size_t)st * p.split_s * BM * BN +
-                     (size_t)(cn * CC + ty) * BM + cm * RC + tx;
+    const uint32_t r0 = cm * RC;                        // chunk's first row in the tile
+    const float* P = p.partial + ((size_t)st * p.split_s * H + r0 / BM) * BM * BN +
+                     (size_t)(cn * CC + ty) * BM + (r0 % BM) + tx;
+    const size_t qstride = (size_t)H * BM * BN;         // next split of the same half
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) acc[j] = __ldcg(P + (size_t)j * 8 * BM);
@@ -591,7 +596,7 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) x[i][j] = __ldcg(P + (size_t)(q + i) * BM * BN + (size_t)j * 8 * BM);
+            for (int j = 0; j < 8; j++) x[i][j] = __ldcg(P + (size_t)(q + i) * qstride + (size_t)j * 8 * BM);
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
@@ -600,13 +605,13 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
     for (; q < p.split_s; q++) {
         float x[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) x[j] = __ldcg(P + (size_t)q * BM * BN + (size_t)j * 8 * BM);
+        for (int j = 0; j < 8; j++) x[j] = __ldcg(P + (size_t)q * qstride + (size_t)j * 8 * BM);
 #pragma unroll
         for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], x[j]);
     }
     TOut* C = reinterpret_cast<TOut*>(p.C) + p.sc * (int64_t)b;
     if (p.c_trans) {            // lanes run along C's rows already: store directly
-        const uint32_t m = mb * BM + cm * RC + tx;
+        const uint32_t m = mb * TILE_ROWS + cm * RC + tx;
         if (m >= p.M) return;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
@@ -624,7 +629,7 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        const uint32_t rl = ty + 8 * j, m = mb * BM + cm * RC + rl;
+        const uint32_t rl = ty + 8 * j, m = mb * TILE_ROWS + cm * RC + rl;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const uint32_t cl = h * 32 + tx, n = nb * BN + cn * CC + cl;
@@ -879,9 +884,9 @@ cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, uint32_t 
 
 // The reduce of split tiles, launched so that it may become resident while
 // the GEMM grid drains (programmatic stream serialization).
-template <typename TOut, int BN>
+template <typename TOut, int BN, int TILE_ROWS = BM>
 cudaError_t launch_reduce(const UmmaParams& prm, cudaStream_t s) {
-    const uint32_t chunks = (prm.total_tiles - prm.full_tiles) * (BM / 32) * (BN / 64);
+    const uint32_t chunks = (prm.total_tiles - prm.full_tiles) * (TILE_ROWS / 32) * (BN / 64);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(chunks);
     cfg.blockDim = dim3(256);
@@ -892,7 +897,7 @@ cudaError_t launch_reduce(const UmmaParams& prm, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, split_reduce_kernel<TOut, BN>, prm);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, split_reduce_kernel<TOut, BN, TILE_ROWS>, prm);
     count_launch();
     return e;
 }
@@ -929,15 +934,20 @@ GemmProblem swapped(const GemmProblem& p) {
     return q;
 }
 
-// The problem the kernel runs and its N tile.
+// The problem the kernel runs, its tile and whether CTA pairs run it (256-row
+// tiles whenever M fills them).
 struct KernelShape {
     GemmProblem q;
     bool c_trans;
     uint32_t BN;
+    bool pair;
+    uint32_t bm_tile;
 };
 KernelShape kernel_shape(const GemmProblem& p) {
-    if (small_m_swap(p)) return {swapped(p), true, (uint32_t)BN_SM};
-    return {p, false, (uint32_t)(p.dtype == DT_F32 ? 128 : BN_16)};
+    if (small_m_swap(p)) return {swapped(p), true, (uint32_t)BN_SM, false, (uint32_t)BM};
+    const bool pair = pair_enabled() && p.M >= 2u * BM;
+    return {p, false, (uint32_t)(p.dtype == DT_F32 ? 128 : BN_16), pair,
+            (uint32_t)(pair ? 2 * BM : BM)};
 }
 constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
 
@@ -963,10 +973,14 @@ SplitPlan plan_split(const KernelShape& ks, int num_sms) {
     // 128 x 64 small-M tiles stream weights (~0.3 us per k-block) and their
     // partial tiles are a quarter of a 128 x 256 tile's.
     const uint32_t min_saved_kb = is32 ? 16u : (BN == (uint32_t)BN_SM ? 8u : 48u);
-    const uint64_t T = (uint64_t)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN) * p.batch;
+    const uint64_t T =
+        (uint64_t)((p.M + ks.bm_tile - 1) / ks.bm_tile) * ((p.N + BN - 1) / BN) * p.batch;
     const uint32_t num_kb = (p.K + BK - 1) / BK;
     SplitPlan pl{(uint32_t)T, 1, num_kb, (uint32_t)T, 0};
-    const uint64_t P = (uint64_t)(num_sms > 0 ? num_sms : 1);
+    // Workers: SMs, or SM pairs for 256-row tiles (the per-SM work of a tile
+    // and its k-block time are the same in both cases).
+    const int workers = ks.pair ? num_sms / 2 : num_sms;
+    const uint64_t P = (uint64_t)(workers > 0 ? workers : 1);
     const uint64_t rem = T % P;
     if (rem == 0 || T >= (1ull << 31)) return pl;
     uint32_t S = (uint32_t)(P / rem);
@@ -982,7 +996,7 @@ SplitPlan plan_split(const KernelShape& ks, int num_sms) {
     pl.s = s2;
     pl.kb_per = kb_per;
     pl.units = pl.full + (uint32_t)rem * s2;
-    pl.partial_bytes = (size_t)rem * s2 * BM * BN * sizeof(float);
+    pl.partial_bytes = (size_t)rem * s2 * ks.bm_tile * BN * sizeof(float);
     return pl;
 }
 
@@ -1020,9 +1034,9 @@ bool umma_profitable(const GemmProblem& p) {
 }
 
 bool umma_uses_pair(const GemmProblem& p, int num_sms, bool split_ws) {
-    const KernelShape ks = kernel_shape(p);
-    const SplitPlan pl = plan_split(ks, num_sms);
-    return pair_enabled() && !ks.c_trans && !(pl.s > 1 && split_ws) && ks.q.M >= 2u * BM;
+    (void)num_sms;
+    (void)split_ws;
+    return kernel_shape(p).pair;
 }
 
 int umma_split_count(const GemmProblem& p, int num_sms) {
@@ -1057,7 +1071,7 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     const uint32_t BK = ROW_BYTES / esize, EPB = ROW_BYTES / esize;
     // 256-row tiles on CTA pairs when no split is planned and M fills them.
     const SplitPlan pl = plan_split(ks, num_sms);
-    const bool pair = umma_uses_pair(p_in, num_sms, split_ws != nullptr);
+    const bool pair = ks.pair;
     const uint32_t bn_cta = pair ? (uint32_t)BN / 2 : (uint32_t)BN;      // B rows per CTA
 
     auto box_for = [&](const Operand& o, uint32_t tile_rows, uint32_t& bi, uint32_t& bo) {
@@ -1122,14 +1136,14 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     prm.ldc = p.ldc;
     prm.sc = p.sc;
     prm.M = p.M; prm.N = p.N; prm.K = p.K; prm.batch = p.batch;
-    const uint32_t bm_tile = pair ? 2u * BM : (uint32_t)BM;
+    const uint32_t bm_tile = ks.bm_tile;
     prm.tiles_m = (p.M + bm_tile - 1) / bm_tile;
     prm.tiles_n = (p.N + BN - 1) / BN;
     prm.num_kb = (p.K + BK - 1) / BK;
     const uint64_t total = (uint64_t)prm.tiles_m * prm.tiles_n * p.batch;
     if (total >= (1ull << 31)) return cudaErrorNotSupported;
     prm.total_tiles = (uint32_t)total;
-    if (!pair && pl.s > 1 && split_ws) {
+    if (pl.s > 1 && split_ws) {
         prm.full_tiles = pl.full;
         prm.split_s = pl.s;
         prm.split_kb = pl.kb_per;
@@ -1170,11 +1184,17 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     }
     if (e != cudaSuccess || prm.split_s <= 1) return e;
     switch (p.dtype) {
-        case DT_F16: return sm ? launch_reduce<__half, BN_SM>(prm, s) : launch_reduce<__half, BN_16>(prm, s);
+        case DT_F16:
+            return sm     ? launch_reduce<__half, BN_SM>(prm, s)
+                   : pair ? launch_reduce<__half, BN_16, 2 * BM>(prm, s)
+                          : launch_reduce<__half, BN_16>(prm, s);
         case DT_BF16:
-            return sm ? launch_reduce<__nv_bfloat16, BN_SM>(prm, s)
-                      : launch_reduce<__nv_bfloat16, BN_16>(prm, s);
-        default: return launch_reduce<float, BN_TF32>(prm, s);
+            return sm     ? launch_reduce<__nv_bfloat16, BN_SM>(prm, s)
+                   : pair ? launch_reduce<__nv_bfloat16, BN_16, 2 * BM>(prm, s)
+                          : launch_reduce<__nv_bfloat16, BN_16>(prm, s);
+        default:
+            return pair ? launch_reduce<float, BN_TF32, 2 * BM>(prm, s)
+                        : launch_reduce<float, BN_TF32>(prm, s);
     }
 }
 
