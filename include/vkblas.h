@@ -103,10 +103,15 @@ vkblas_status_t vkblas_gemm_f16(
     uint32_t batch,
     int64_t stride_a, int64_t stride_b, int64_t stride_c);
 
-/* reference src/vkblas.h:79-88, 92-100, 105-114.  complex64 / fp64 /
- * complex128 are outside this build's kernels: these return non-zero, which
- * the reference defines as "engine unavailable, caller forwards to the real
- * library" (the hipBLAS shim does exactly that). */
+/* reference src/vkblas.h:79-88, 92-100, 105-114.  Same row-major contract
+ * as the others, on the thread's vkblas stream; A, B and C are complex
+ * interleaved (8- or 16-byte elements) or double, ld and strides in
+ * elements, alpha / beta by value.  fp64 runs an exact fp64 GEMM (one fma per
+ * k in order, then alpha*acc + beta*C); complex64 / complex128 run four real
+ * GEMMs on planar copies plus a combine, as the reference does
+ * (src/vkblas.c:3748-3930).  Returns 0 when done, non-zero when not run
+ * (invalid arguments, no usable GPU): the caller then forwards to a real
+ * library, as the reference defines. */
 int vkblas_gemm_c64(
     vkblas_op_t op_a, vkblas_op_t op_b,
     uint32_t M, uint32_t N, uint32_t K,

@@ -176,9 +176,12 @@ hipblasStatus_t hipblasGemmEx(hipblasHandle_t handle, hipblasOperation_t transA,
                               hipblasDatatype_t cType, int ldc,
                               vkblas_gemmex_compute_t computeType, hipblasGemmAlgo_t algo);
 
-/* ---------------------------------- forward-only GEMMs (fp64 / complex)
- * reference src/vkblas_hipblas.c:467-630: the reference ran these on its own
- * fp64/complex shaders; here the engine declines and the call is forwarded. */
+/* ---------------------------------------- fp64 / complex GEMMs
+ * reference src/vkblas_hipblas.c:470-620.  Run on vkblas_gemm_{f64,c64,z64}
+ * (operands swapped into the engine's row-major contract) on the handle's
+ * stream; forwarded to the real library when the engine declines.  Scalars
+ * in device memory (pointer mode DEVICE) are read with one blocking copy; a
+ * conjugate transpose (HIPBLAS_OP_C) of a complex operand is forwarded. */
 hipblasStatus_t hipblasDgemm(hipblasHandle_t handle, hipblasOperation_t transA,
                              hipblasOperation_t transB, int m, int n, int k, const double* alpha,
                              const double* AP, int lda, const double* BP, int ldb,

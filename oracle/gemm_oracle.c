@@ -31,6 +31,10 @@
  *     what this library's kernels do), or the reference reduce's own encoders
  *     (rounding 1: packHalf2x16 RNE for fp16, truncation to the upper 16 bits
  *     for bf16 -- splitk_reduce_half.comp:5,8, splitk_reduce_m_half.comp:6,9).
+ *   - orc_dgemm_rowmajor_seq, orc_cgemm_rowmajor, orc_zgemm_rowmajor: the
+ *     fp64 and complex fallbacks (src/vkblas.c:3653-4188): sequential fma in
+ *     double; complex as four real GEMMs on planar copies plus the combine of
+ *     cx_combine.comp / cx_combine_d64.comp.
  *   - orc_gemm_rowmajor_f32_splitk: the same segment model for fp32 (the
  *     decode matvec with K x N weights, matvec_f32_tmpl.comp TB=0).
  *   - f16/bf16 converters: exact RNE (what packHalf2x16 and the GPU's
@@ -204,6 +208,89 @@ EXPORT void orc_gemm_rowmajor_f32_splitk(int op_a, int op_b, uint32_t M, uint32_
             float t2 = beta * old;
             *c = t1 + t2;
         }
+}
+
+/* fp64 engine contract (gemm_f64_32x32_tmpl.comp:85-117): one double
+ * accumulator per output, k in order with fma, then alpha*acc + beta*c with
+ * separate roundings (c not read when beta == 0). */
+EXPORT void orc_dgemm_rowmajor_seq(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K,
+                                   double alpha, const double* A, uint32_t lda,
+                                   const double* B, uint32_t ldb, double beta, double* C,
+                                   uint32_t ldc, uint32_t batch, int64_t sa, int64_t sb,
+                                   int64_t sc) {
+    for (uint32_t b = 0; b < batch; b++) {
+        const double* Ab = A + sa * (int64_t)b;
+        const double* Bb = B + sb * (int64_t)b;
+        double* Cb = C + sc * (int64_t)b;
+        for (uint32_t m = 0; m < M; m++)
+            for (uint32_t n = 0; n < N; n++) {
+                double acc = 0.0;
+                for (uint32_t k = 0; k < K; k++)
+                    acc = fma(Ab[a_idx(op_a, m, k, lda)], Bb[b_idx(op_b, k, n, ldb)], acc);
+                double* c = &Cb[(size_t)m * ldc + n];
+                double old = beta != 0.0 ? *c : 0.0;
+                double t1 = alpha * acc;
+                double t2 = beta * old;
+                *c = t1 + t2;
+            }
+    }
+}
+
+/* Complex GEMM the reference's way (src/vkblas.c:3748-3930, 4092-4188):
+ * interleaved A, B, C split into real / imaginary planes at the same element
+ * offsets, four real GEMMs
+ *   T1 = Ar*Br;  T1 = -1*(Ai*Bi) + 1*T1;  T2 = Ar*Bi;  T2 = 1*(Ai*Br) + 1*T2
+ * in the sequential engine contract (fp32 for complex64, fp64 for
+ * complex128), then the combine of cx_combine.comp:32-45, left to right:
+ *   C.r = ar*T1 - ai*T2 + br*C.r - bi*C.i,  C.i = ar*T2 + ai*T1 + br*C.i + bi*C.r
+ * (the beta terms only when beta != 0). */
+static size_t span_of(uint32_t rows, uint32_t cols, uint32_t ld, uint32_t batch, int64_t stride) {
+    return (batch > 1 ? (size_t)stride * (batch - 1) : 0) + (size_t)(rows - 1) * ld + cols;
+}
+
+#define CX_GEMM_BODY(T, GEMM)                                                                  \
+    uint32_t ra = op_a ? K : M, ca = op_a ? M : K, rb = op_b ? N : K, cb = op_b ? K : N;       \
+    size_t ea = span_of(ra, ca, lda, batch, sa), eb = span_of(rb, cb, ldb, batch, sb);         \
+    size_t ec = span_of(M, N, ldc, batch, sc);                                                 \
+    T* Ar = (T*)calloc(ea, sizeof(T)); T* Ai = (T*)calloc(ea, sizeof(T));                      \
+    T* Br = (T*)calloc(eb, sizeof(T)); T* Bi = (T*)calloc(eb, sizeof(T));                      \
+    T* T1 = (T*)calloc(ec, sizeof(T)); T* T2 = (T*)calloc(ec, sizeof(T));                      \
+    for (size_t i = 0; i < ea; i++) { Ar[i] = A[2 * i]; Ai[i] = A[2 * i + 1]; }                \
+    for (size_t i = 0; i < eb; i++) { Br[i] = B[2 * i]; Bi[i] = B[2 * i + 1]; }                \
+    GEMM(op_a, op_b, M, N, K, 1, Ar, lda, Br, ldb, 0, T1, ldc, batch, sa, sb, sc);             \
+    GEMM(op_a, op_b, M, N, K, -1, Ai, lda, Bi, ldb, 1, T1, ldc, batch, sa, sb, sc);            \
+    GEMM(op_a, op_b, M, N, K, 1, Ar, lda, Bi, ldb, 0, T2, ldc, batch, sa, sb, sc);             \
+    GEMM(op_a, op_b, M, N, K, 1, Ai, lda, Br, ldb, 1, T2, ldc, batch, sa, sb, sc);             \
+    for (uint32_t b = 0; b < batch; b++)                                                       \
+        for (uint32_t m = 0; m < M; m++)                                                       \
+            for (uint32_t n = 0; n < N; n++) {                                                 \
+                size_t o = (size_t)(sc * (int64_t)b) + (size_t)m * ldc + n;                    \
+                T fr = T1[o], fi = T2[o], outr, outi;                                          \
+                if (br != 0 || bi != 0) {                                                      \
+                    T r0 = C[2 * o], i0 = C[2 * o + 1];                                        \
+                    outr = ar * fr - ai * fi + br * r0 - bi * i0;                              \
+                    outi = ar * fi + ai * fr + br * i0 + bi * r0;                              \
+                } else {                                                                       \
+                    outr = ar * fr - ai * fi;                                                  \
+                    outi = ar * fi + ai * fr;                                                  \
+                }                                                                              \
+                C[2 * o] = outr;                                                               \
+                C[2 * o + 1] = outi;                                                           \
+            }                                                                                  \
+    free(Ar); free(Ai); free(Br); free(Bi); free(T1); free(T2);
+
+EXPORT void orc_cgemm_rowmajor(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K, float ar,
+                               float ai, const float* A, uint32_t lda, const float* B,
+                               uint32_t ldb, float br, float bi, float* C, uint32_t ldc,
+                               uint32_t batch, int64_t sa, int64_t sb, int64_t sc) {
+    CX_GEMM_BODY(float, orc_gemm_rowmajor_f32seq)
+}
+
+EXPORT void orc_zgemm_rowmajor(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K, double ar,
+                               double ai, const double* A, uint32_t lda, const double* B,
+                               uint32_t ldb, double br, double bi, double* C, uint32_t ldc,
+                               uint32_t batch, int64_t sa, int64_t sb, int64_t sc) {
+    CX_GEMM_BODY(double, orc_dgemm_rowmajor_seq)
 }
 
 /* Double-precision product of the same contract, written to a separate

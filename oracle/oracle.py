@@ -53,6 +53,12 @@ def _load():
                                               _u16p, _u32, _f, _u16p, _u32, _i]
     lib.orc_gemm_rowmajor_f32_splitk.argtypes = [_i, _i, _u32, _u32, _u32, _u32, _f, _f32p, _u32,
                                                  _f32p, _u32, _f, _f32p, _u32]
+    lib.orc_dgemm_rowmajor_seq.argtypes = [_i, _i, _u32, _u32, _u32, _d, _f64p, _u32, _f64p, _u32,
+                                           _d, _f64p, _u32, _u32, _i64, _i64, _i64]
+    lib.orc_cgemm_rowmajor.argtypes = [_i, _i, _u32, _u32, _u32, _f, _f, _f32p, _u32, _f32p, _u32,
+                                       _f, _f, _f32p, _u32, _u32, _i64, _i64, _i64]
+    lib.orc_zgemm_rowmajor.argtypes = [_i, _i, _u32, _u32, _u32, _d, _d, _f64p, _u32, _f64p, _u32,
+                                       _d, _d, _f64p, _u32, _u32, _i64, _i64, _i64]
     lib.orc_gen_test_gemm.argtypes = [C.c_uint, _f32p, _sz, _f32p, _sz, _f32p, _sz]
     lib.orc_gen_test_h.argtypes = [C.c_uint, _i, _u16p, _sz, _u16p, _sz, _u16p, _sz, _i]
     lib.orc_sgemm_colmajor_rows_mt.argtypes = [_i, _i, _i, _i, _i, _f, _f32p, _i, _f32p, _i, _f,
@@ -169,6 +175,27 @@ def gemm_rowmajor_f32_splitk(op_a, op_b, M, N, K, span, alpha, A, lda, B, ldb, b
     """fp32 split-K model: segments of `span` k, each a sequential fmaf sum,
     added in segment order, then the fp32 epilogue (C updated in place)."""
     lib.orc_gemm_rowmajor_f32_splitk(op_a, op_b, M, N, K, span, alpha, A, lda, B, ldb, beta, C, ldc)
+
+
+def dgemm_rowmajor_seq(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, batch=1,
+                       sa=0, sb=0, sc=0):
+    """fp64 engine contract, sequential fma; C (float64) updated in place."""
+    lib.orc_dgemm_rowmajor_seq(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, batch,
+                               sa, sb, sc)
+
+
+def cgemm_rowmajor(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, batch=1, sa=0, sb=0,
+                   sc=0):
+    """complex64 the reference's way (interleaved float32 arrays, C in place)."""
+    lib.orc_cgemm_rowmajor(op_a, op_b, M, N, K, alpha.real, alpha.imag, A, lda, B, ldb, beta.real,
+                           beta.imag, C, ldc, batch, sa, sb, sc)
+
+
+def zgemm_rowmajor(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, batch=1, sa=0, sb=0,
+                   sc=0):
+    """complex128 the reference's way (interleaved float64 arrays, C in place)."""
+    lib.orc_zgemm_rowmajor(op_a, op_b, M, N, K, alpha.real, alpha.imag, A, lda, B, ldb, beta.real,
+                           beta.imag, C, ldc, batch, sa, sb, sc)
 
 
 # -------------------------------------------------------------- generators

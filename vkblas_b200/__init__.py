@@ -55,6 +55,15 @@ def _load() -> C.CDLL:
     lib.vkblas_gemv_splitk_noalloc.argtypes = [i32, u32, u32, u32, f32, vp, u32, vp, u32, f32, vp,
                                                u32, u32, vp]
     lib.vkblas_gemv_splitk_noalloc.restype = i32
+    f64 = C.c_double
+    lib.vkblas_gemm_f64.argtypes = [i32, i32, u32, u32, u32, f64, vp, u32, vp, u32, f64, vp, u32,
+                                    u32, i64, i64, i64]
+    lib.vkblas_gemm_c64.argtypes = [i32, i32, u32, u32, u32, f32, f32, vp, u32, vp, u32, f32, f32,
+                                    vp, u32, u32, i64, i64, i64]
+    lib.vkblas_gemm_z64.argtypes = [i32, i32, u32, u32, u32, f64, f64, vp, u32, vp, u32, f64, f64,
+                                    vp, u32, u32, i64, i64, i64]
+    for name in ("vkblas_gemm_f64", "vkblas_gemm_c64", "vkblas_gemm_z64"):
+        getattr(lib, name).restype = i32
     lib.vkblas_set_stream.argtypes = [vp]
     lib.vkblas_get_stream.restype = vp
     lib.vkblas_b200_set_path.argtypes = [i32]

@@ -99,6 +99,16 @@ cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, v
 // entry point is missing or the layout cannot be described.
 bool encode_tmap_2d(CUtensorMap* m, bool bf16, const void* base, uint64_t inner, uint64_t outer,
                     uint64_t ld, uint32_t box_inner, uint32_t box_outer);
+// fp64 GEMM (exact sequential fma) and the complex planar helpers (dgemm.cu).
+cudaError_t launch_dgemm(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K, double alpha,
+                         const double* A, uint32_t lda, const double* B, uint32_t ldb, double beta,
+                         double* C, uint32_t ldc, uint32_t batch, int64_t sa, int64_t sb,
+                         int64_t sc, cudaStream_t s);
+cudaError_t launch_cx_split(bool dbl, const void* src, uint32_t rows, uint32_t cols, uint32_t ld,
+                            int64_t stride, uint32_t batch, void* re, void* im, cudaStream_t s);
+cudaError_t launch_cx_combine(bool dbl, const void* t1, const void* t2, void* C, uint32_t M,
+                              uint32_t N, uint32_t ldc, int64_t sc, uint32_t batch, double ar,
+                              double ai, double br, double bi, cudaStream_t s);
 // Host-side launch counter (all kernels of this library).
 void count_launch();
 }  // namespace vkb

@@ -1,0 +1,192 @@
+// dgemm.cu -- fp64 GEMM and the complex64 / complex128 helpers.
+//
+// Replaces the reference's fp64 and complex fallbacks (lakitu12/vkblas
+// src/vkblas.c:3653-4188, shaders gemm_f64_32x32_tmpl.comp, cvt_cx.comp,
+// cvt_cz.comp, cx_combine.comp, cx_combine_d64.comp):
+//   - fp64 GEMM: every output owns one double accumulator, k in increasing
+//     order with one fused multiply-add per step (gemm_f64_32x32_tmpl.comp:
+//     85-100), then C = alpha*acc + beta*C with separate roundings, C not read
+//     when beta == 0 (:116-117).  Bit-identical to the sequential fma oracle.
+//   - complex GEMMs run as four real GEMMs on planar copies (the engine's
+//     fp32 GEMM for complex64, the kernel below for complex128):
+//       T1 = Ar*Br;  T1 = -1*(Ai*Bi) + 1*T1;  T2 = Ar*Bi;  T2 = 1*(Ai*Br) + 1*T2
+//     (vkblas.c:3816-3823), then the combine
+//       C.r = ar*T1 - ai*T2 + br*C.r - bi*C.i,  C.i = ar*T2 + ai*T1 + br*C.i + bi*C.r
+//     left to right with separate roundings, the beta terms only when beta is
+//     non-zero (cx_combine.comp:32-45).
+// Planar copies keep the interleaved operand's element offsets (ld and batch
+// stride), so the real GEMMs read them with the caller's leading dimensions.
+#include "common.cuh"
+
+namespace vkb {
+namespace {
+
+constexpr int DT = 64, DBK = 8, DTHREADS = 256;   // 64x64 tile, 4x4 outputs per thread
+
+struct DArgs {
+    int op_a, op_b;
+    uint32_t M, N, K;
+    double alpha, beta;
+    const double* A; uint32_t lda;
+    const double* B; uint32_t ldb;
+    double* C; uint32_t ldc;
+    int64_t sa, sb, sc;
+};
+
+// Thread (tx, ty) of a 16 x 16 layout owns rows ty + 16 i and columns
+// tx + 16 j of the tile: shared-memory reads are consecutive doubles across
+// the warp and C stores are coalesced along n.
+__global__ void __launch_bounds__(DTHREADS) dgemm_kernel(DArgs a) {
+    __shared__ double As[DBK][DT + 1];     // [k][m]
+    __shared__ double Bs[DBK][DT + 1];     // [k][n]
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const uint32_t b = blockIdx.z, m0 = blockIdx.y * DT, n0 = blockIdx.x * DT;
+    const double* A = a.A + a.sa * (int64_t)b;
+    const double* B = a.B + a.sb * (int64_t)b;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+    for (uint32_t k0 = 0; k0 < a.K; k0 += DBK) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int e = tid * 2 + h;                     // 512 elements per operand tile
+            uint32_t m, k;
+            if (a.op_a == 0) { m = e >> 3; k = e & 7; }     // A[m*lda + k]: along k
+            else { k = e >> 6; m = e & 63; }                // A[k*lda + m]: along m
+            const uint32_t gm = m0 + m, gk = k0 + k;
+            As[k][m] = (gm < a.M && gk < a.K)
+                           ? (a.op_a == 0 ? A[(size_t)gm * a.lda + gk] : A[(size_t)gk * a.lda + gm])
+                           : 0.0;
+            uint32_t n, kb;
+            if (a.op_b == 0) { kb = e >> 6; n = e & 63; }   // B[k*ldb + n]: along n
+            else { n = e >> 3; kb = e & 7; }                // B[n*ldb + k]: along k
+            const uint32_t gn = n0 + n, gkb = k0 + kb;
+            Bs[kb][n] = (gn < a.N && gkb < a.K)
+                            ? (a.op_b == 0 ? B[(size_t)gkb * a.ldb + gn] : B[(size_t)gn * a.ldb + gkb])
+                            : 0.0;
+        }
+        __syncthreads();
+        const uint32_t kend = min((uint32_t)DBK, a.K - k0);   // stop at K: no extra terms
+        for (uint32_t kk = 0; kk < kend; kk++) {
+            double av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) av[i] = As[kk][ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) bv[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = __fma_rn(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+    double* C = a.C + a.sc * (int64_t)b;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t m = m0 + ty + 16 * i;
+        if (m >= a.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t n = n0 + tx + 16 * j;
+            if (n >= a.N) continue;
+            double* c = C + (size_t)m * a.ldc + n;
+            const double old = (a.beta != 0.0) ? *c : 0.0;
+            *c = __dadd_rn(__dmul_rn(a.alpha, acc[i][j]), __dmul_rn(a.beta, old));
+        }
+    }
+}
+
+// Interleaved complex [b*stride + r*ld + c] -> real and imaginary planes at
+// the same element offsets, for r < rows, c < cols.
+template <typename T>
+__global__ void cx_split_kernel(const T* __restrict__ src, uint32_t rows, uint32_t cols,
+                                uint32_t ld, int64_t stride, T* __restrict__ re,
+                                T* __restrict__ im) {
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    for (uint32_t r = blockIdx.y; r < rows; r += gridDim.y) {
+        const size_t o = (size_t)(stride * (int64_t)blockIdx.z) + (size_t)r * ld + c;
+        re[o] = src[2 * o];
+        im[o] = src[2 * o + 1];
+    }
+}
+
+__device__ __forceinline__ float mul_rn(float x, float y) { return __fmul_rn(x, y); }
+__device__ __forceinline__ double mul_rn(double x, double y) { return __dmul_rn(x, y); }
+__device__ __forceinline__ float add_rn(float x, float y) { return __fadd_rn(x, y); }
+__device__ __forceinline__ double add_rn(double x, double y) { return __dadd_rn(x, y); }
+__device__ __forceinline__ float sub_rn(float x, float y) { return __fsub_rn(x, y); }
+__device__ __forceinline__ double sub_rn(double x, double y) { return __dsub_rn(x, y); }
+
+// C = alpha * (T1 + i T2) + beta * C over M x N per batch entry (C interleaved).
+template <typename T>
+__global__ void cx_combine_kernel(const T* __restrict__ t1, const T* __restrict__ t2, T* C,
+                                  uint32_t M, uint32_t N, uint32_t ldc, int64_t sc, T ar, T ai,
+                                  T br, T bi) {
+    const uint32_t n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    for (uint32_t m = blockIdx.y; m < M; m += gridDim.y) {
+        const size_t o = (size_t)(sc * (int64_t)blockIdx.z) + (size_t)m * ldc + n;
+        const T fr = t1[o], fi = t2[o];
+        T outr = sub_rn(mul_rn(ar, fr), mul_rn(ai, fi));
+        T outi = add_rn(mul_rn(ar, fi), mul_rn(ai, fr));
+        if (br != T(0) || bi != T(0)) {
+            const T r0 = C[2 * o], i0 = C[2 * o + 1];
+            outr = sub_rn(add_rn(outr, mul_rn(br, r0)), mul_rn(bi, i0));
+            outi = add_rn(add_rn(outi, mul_rn(br, i0)), mul_rn(bi, r0));
+        }
+        C[2 * o] = outr;
+        C[2 * o + 1] = outi;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_dgemm(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K, double alpha,
+                         const double* A, uint32_t lda, const double* B, uint32_t ldb, double beta,
+                         double* C, uint32_t ldc, uint32_t batch, int64_t sa, int64_t sb,
+                         int64_t sc, cudaStream_t s) {
+    DArgs a{op_a, op_b, M, N, K, alpha, beta, A, lda, B, ldb, C, ldc, sa, sb, sc};
+    const dim3 grid((N + DT - 1) / DT, (M + DT - 1) / DT, batch);
+    if (grid.y > 65535 || grid.z > 65535) return cudaErrorInvalidConfiguration;
+    dgemm_kernel<<<grid, DTHREADS, 0, s>>>(a);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cx_split(bool dbl, const void* src, uint32_t rows, uint32_t cols, uint32_t ld,
+                            int64_t stride, uint32_t batch, void* re, void* im, cudaStream_t s) {
+    const dim3 grid((cols + 255) / 256, rows < 65535u ? rows : 65535u, stride ? batch : 1);
+    if (grid.z > 65535) return cudaErrorInvalidConfiguration;
+    if (dbl)
+        cx_split_kernel<double><<<grid, 256, 0, s>>>(static_cast<const double*>(src), rows, cols,
+                                                       ld, stride, static_cast<double*>(re),
+                                                       static_cast<double*>(im));
+    else
+        cx_split_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(src), rows, cols, ld,
+                                                      stride, static_cast<float*>(re),
+                                                      static_cast<float*>(im));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cx_combine(bool dbl, const void* t1, const void* t2, void* C, uint32_t M,
+                              uint32_t N, uint32_t ldc, int64_t sc, uint32_t batch, double ar,
+                              double ai, double br, double bi, cudaStream_t s) {
+    const dim3 grid((N + 255) / 256, M < 65535u ? M : 65535u, batch);
+    if (grid.z > 65535) return cudaErrorInvalidConfiguration;
+    if (dbl)
+        cx_combine_kernel<double><<<grid, 256, 0, s>>>(
+            static_cast<const double*>(t1), static_cast<const double*>(t2), static_cast<double*>(C),
+            M, N, ldc, sc, ar, ai, br, bi);
+    else
+        cx_combine_kernel<float><<<grid, 256, 0, s>>>(
+            static_cast<const float*>(t1), static_cast<const float*>(t2), static_cast<float*>(C), M,
+            N, ldc, sc, (float)ar, (float)ai, (float)br, (float)bi);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace vkb

@@ -78,8 +78,8 @@ struct DeviceState {
     int* d_status = nullptr;
     std::mutex mu;
     // [0]: GEMV split-K (partials + zero-initialised tickets), [1]: 3xTF32 operand planes,
-    // [2]: tcgen05 split-K partial tiles.
-    std::unordered_map<cudaStream_t, Workspace> ws[3];
+    // [2]: tcgen05 split-K partial tiles, [3]: complex GEMM planes.
+    std::unordered_map<cudaStream_t, Workspace> ws[4];
 };
 
 std::mutex g_dev_mu;
@@ -329,22 +329,119 @@ VKB_EXPORT vkblas_status_t vkblas_gemm_bf16_hipblas(vkblas_op_t op_a, vkblas_op_
                             stride_a, stride_b, stride_c);
 }
 
-VKB_EXPORT int vkblas_gemm_c64(vkblas_op_t, vkblas_op_t, uint32_t, uint32_t, uint32_t, float,
-                               float, const void*, uint32_t, const void*, uint32_t, float, float,
-                               void*, uint32_t, uint32_t, int64_t, int64_t, int64_t) {
-    return VKBLAS_ERR_FALLBACK;
+// ---------------------------------------------- fp64 and complex GEMMs
+// Reference src/vkblas.c:3748-4188: fp64 runs one exact fp64 GEMM; complex64
+// and complex128 run four real GEMMs on planar copies and a combine (see
+// dgemm.cu for the arithmetic).  0 = done; non-zero = not run (the caller
+// forwards to a real library), as in the reference.
+
+namespace {
+
+// Elements an operand spans: (batch - 1) * stride + (rows - 1) * ld + cols.
+size_t extent(uint32_t rows, uint32_t cols, uint32_t ld, uint32_t batch, int64_t stride) {
+    return (size_t)(batch > 1 ? (size_t)stride * (batch - 1) : 0) + (size_t)(rows - 1) * ld + cols;
 }
 
-VKB_EXPORT int vkblas_gemm_f64(vkblas_op_t, vkblas_op_t, uint32_t, uint32_t, uint32_t, double,
-                               const void*, uint32_t, const void*, uint32_t, double, void*,
-                               uint32_t, uint32_t, int64_t, int64_t, int64_t) {
-    return VKBLAS_ERR_FALLBACK;
+DeviceState* current_device(cudaStream_t& s) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    DeviceState* ds = device_state(dev);
+    if (!ds || ds->cc_major != 10) return nullptr;
+    s = reinterpret_cast<cudaStream_t>(tls.stream);
+    return ds;
 }
 
-VKB_EXPORT int vkblas_gemm_z64(vkblas_op_t, vkblas_op_t, uint32_t, uint32_t, uint32_t, double,
-                               double, const void*, uint32_t, const void*, uint32_t, double,
-                               double, void*, uint32_t, uint32_t, int64_t, int64_t, int64_t) {
-    return VKBLAS_ERR_FALLBACK;
+bool valid_batched(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, const void* A,
+                   const void* B, const void* C, int64_t sa, int64_t sb, int64_t sc) {
+    return M && N && K && batch && A && B && C && sa >= 0 && sb >= 0 && sc >= 0;
+}
+
+// Complex GEMM through planar copies: four real GEMMs (fp32 engine calls or
+// fp64 kernels) and the combine, all on stream s.
+int complex_gemm(bool dbl, vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M, uint32_t N, uint32_t K,
+                 double ar, double ai, const void* A, uint32_t lda, const void* B, uint32_t ldb,
+                 double br, double bi, void* C, uint32_t ldc, uint32_t batch, int64_t sa,
+                 int64_t sb, int64_t sc) {
+    if (!valid_batched(M, N, K, batch, A, B, C, sa, sb, sc)) return 1;
+    cudaStream_t s;
+    DeviceState* ds = current_device(s);
+    if (!ds) return 1;
+    const size_t es = dbl ? 8 : 4;
+    const uint32_t ra = op_a ? K : M, ca = op_a ? M : K;
+    const uint32_t rb = op_b ? N : K, cb = op_b ? K : N;
+    const size_t ea = extent(ra, ca, lda, batch, sa), eb = extent(rb, cb, ldb, batch, sb);
+    const size_t ec = extent(M, N, ldc, batch, sc);
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t need = 2 * (up(ea * es) + up(eb * es) + up(ec * es));
+    char* w = static_cast<char*>(workspace(ds, 3, s, need));
+    if (!w) return 1;
+    void* Ar = w;
+    void* Ai = w + up(ea * es);
+    void* Br = w + 2 * up(ea * es);
+    void* Bi = static_cast<char*>(Br) + up(eb * es);
+    void* T1 = static_cast<char*>(Bi) + up(eb * es);
+    void* T2 = static_cast<char*>(T1) + up(ec * es);
+    if (launch_cx_split(dbl, A, ra, ca, lda, sa, batch, Ar, Ai, s) != cudaSuccess ||
+        launch_cx_split(dbl, B, rb, cb, ldb, sb, batch, Br, Bi, s) != cudaSuccess)
+        return 1;
+    // T1 = Ar Br; T1 = -(Ai Bi) + T1; T2 = Ar Bi; T2 = Ai Br + T2  (src/vkblas.c:3816-3823)
+    const void* As[4] = {Ar, Ai, Ar, Ai};
+    const void* Bs[4] = {Br, Bi, Bi, Br};
+    void* Cs[4] = {T1, T1, T2, T2};
+    const double al[4] = {1.0, -1.0, 1.0, 1.0}, be[4] = {0.0, 1.0, 0.0, 1.0};
+    for (int i = 0; i < 4; i++) {
+        if (dbl) {
+            if (launch_dgemm(op_a, op_b, M, N, K, al[i], static_cast<const double*>(As[i]), lda,
+                             static_cast<const double*>(Bs[i]), ldb, be[i],
+                             static_cast<double*>(Cs[i]), ldc, batch, sa, sb, sc, s) != cudaSuccess)
+                return 1;
+        } else {
+            GemmProblem p = make_problem(DT_F32, op_a, op_b, M, N, K, (float)al[i], As[i], lda, Bs[i],
+                                         ldb, (float)be[i], Cs[i], ldc, batch, sa, sb, sc);
+            if (run(p, s) != VKBLAS_OK) return 1;
+        }
+    }
+    return launch_cx_combine(dbl, T1, T2, C, M, N, ldc, sc, batch, ar, ai, br, bi, s) == cudaSuccess
+               ? 0
+               : 1;
+}
+
+}  // namespace
+
+VKB_EXPORT int vkblas_gemm_c64(vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M, uint32_t N,
+                               uint32_t K, float alpha_r, float alpha_i, const void* A,
+                               uint32_t lda, const void* B, uint32_t ldb, float beta_r,
+                               float beta_i, void* C, uint32_t ldc, uint32_t batch,
+                               int64_t stride_a, int64_t stride_b, int64_t stride_c) {
+    return complex_gemm(false, op_a, op_b, M, N, K, alpha_r, alpha_i, A, lda, B, ldb, beta_r,
+                        beta_i, C, ldc, batch, stride_a, stride_b, stride_c);
+}
+
+VKB_EXPORT int vkblas_gemm_f64(vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M, uint32_t N,
+                               uint32_t K, double alpha, const void* A, uint32_t lda,
+                               const void* B, uint32_t ldb, double beta, void* C, uint32_t ldc,
+                               uint32_t batch, int64_t stride_a, int64_t stride_b,
+                               int64_t stride_c) {
+    if (!valid_batched(M, N, K, batch, A, B, C, stride_a, stride_b, stride_c)) return 1;
+    cudaStream_t s;
+    if (!current_device(s)) return 1;
+    return launch_dgemm(op_a, op_b, M, N, K, alpha, static_cast<const double*>(A), lda,
+                        static_cast<const double*>(B), ldb, beta, static_cast<double*>(C), ldc,
+                        batch, stride_a, stride_b, stride_c, s) == cudaSuccess
+               ? 0
+               : 1;
+}
+
+VKB_EXPORT int vkblas_gemm_z64(vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M, uint32_t N,
+                               uint32_t K, double alpha_r, double alpha_i, const void* A,
+                               uint32_t lda, const void* B, uint32_t ldb, double beta_r,
+                               double beta_i, void* C, uint32_t ldc, uint32_t batch,
+                               int64_t stride_a, int64_t stride_b, int64_t stride_c) {
+    return complex_gemm(true, op_a, op_b, M, N, K, alpha_r, alpha_i, A, lda, B, ldb, beta_r, beta_i,
+                        C, ldc, batch, stride_a, stride_b, stride_c);
 }
 
 VKB_EXPORT vkblas_status_t vkblas_gemm_ex(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op_t op_b,

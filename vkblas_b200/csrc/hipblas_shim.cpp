@@ -11,6 +11,7 @@
 //
 // VKBLAS_REAL_HIPBLAS / VKBLAS_REAL_ROCBLAS name the real libraries to forward
 // to (defaults: libhipblas.so.2 / librocblas.so.4, as in the reference).
+#include <cuda_runtime_api.h>
 #include <dlfcn.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -350,12 +351,95 @@ SHIM_EXPORT hipblasStatus_t hipblasGemmEx(hipblasHandle_t handle, hipblasOperati
                  ldb, beta, C, cType, ldc, computeType, algo);
 }
 
-// --------------------------------------------- fp64 / complex GEMMs: forward
+// ------------------------------------------------ fp64 / complex GEMMs
+// src/vkblas_hipblas.c:470-620: run on vkblas_gemm_{f64,c64,z64} (engine
+// contract, operands swapped), forward when the engine declines.  Two
+// deliberate differences: scalars in device memory are read with one
+// blocking copy on the handle's stream (the reference dereferences them on
+// the host whatever the pointer mode), and a conjugate transpose of a complex
+// operand is forwarded (the reference passed HIPBLAS_OP_C on as no transpose,
+// src/vkblas_hipblas.c:545-546; this library has no conjugating kernel).
 #define CHECK_MNK(m, n, k)                                                        \
     do {                                                                          \
         if (!as_hip(handle)) return HIPBLAS_STATUS_INVALID_VALUE;                 \
         if ((m) <= 0 || (n) <= 0 || (k) <= 0) return HIPBLAS_STATUS_INVALID_VALUE; \
     } while (0)
+
+namespace {
+
+template <typename T>
+bool host_scalars(const ShimHandle* h, const T* alpha, const T* beta, T& a, T& b) {
+    if (!alpha || !beta) return false;
+    if (h->pointer_mode != HIPBLAS_POINTER_MODE_DEVICE) {
+        a = *alpha;
+        b = *beta;
+        return true;
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(h->stream);
+    if (cudaMemcpyAsync(&a, alpha, sizeof(T), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyAsync(&b, beta, sizeof(T), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return true;
+}
+
+// The engine's fp64 / complex entry points use the thread's vkblas stream:
+// point it at the handle's stream for the call.
+struct OnStream {
+    void* saved;
+    explicit OnStream(const ShimHandle* h) : saved(vkblas_get_stream()) {
+        vkblas_set_stream(reinterpret_cast<void*>(h->stream));
+    }
+    ~OnStream() { vkblas_set_stream(saved); }
+};
+
+// Engine ops for complex operands: N and T only.
+bool cx_ops(int transA, int transB, int& oa, int& ob) {
+    auto op = [](int t) { return t == HIPBLAS_OP_N ? 0 : t == HIPBLAS_OP_T ? 1 : -1; };
+    oa = op(transB);
+    ob = op(transA);
+    return oa >= 0 && ob >= 0;
+}
+
+bool run_d(const ShimHandle* h, int transA, int transB, int m, int n, int k, const double* alpha,
+           const double* A, int lda, long long sA, const double* B, int ldb, long long sB,
+           const double* beta, double* C, int ldc, long long sC, int batch) {
+    const int oa = eng_op(transB), ob = eng_op(transA);
+    double a, b;
+    if (oa < 0 || ob < 0 || lda <= 0 || ldb <= 0 || ldc <= 0 || !host_scalars(h, alpha, beta, a, b))
+        return false;
+    OnStream on(h);
+    return vkblas_gemm_f64((vkblas_op_t)oa, (vkblas_op_t)ob, (uint32_t)n, (uint32_t)m, (uint32_t)k,
+                           a, B, (uint32_t)ldb, A, (uint32_t)lda, b, C, (uint32_t)ldc,
+                           (uint32_t)batch, batch > 1 ? sB : 0, batch > 1 ? sA : 0,
+                           batch > 1 ? sC : 0) == 0;
+}
+
+template <typename CT>
+bool run_cx(const ShimHandle* h, int transA, int transB, int m, int n, int k, const CT* alpha,
+            const CT* A, int lda, long long sA, const CT* B, int ldb, long long sB, const CT* beta,
+            CT* C, int ldc, long long sC, int batch) {
+    int oa, ob;
+    CT a, b;
+    if (!cx_ops(transA, transB, oa, ob) || lda <= 0 || ldb <= 0 || ldc <= 0 ||
+        !host_scalars(h, alpha, beta, a, b))
+        return false;
+    OnStream on(h);
+    const uint32_t sb_ = (uint32_t)batch;
+    if (sizeof(a.x) == 4)
+        return vkblas_gemm_c64((vkblas_op_t)oa, (vkblas_op_t)ob, (uint32_t)n, (uint32_t)m,
+                               (uint32_t)k, (float)a.x, (float)a.y, B, (uint32_t)ldb, A,
+                               (uint32_t)lda, (float)b.x, (float)b.y, C, (uint32_t)ldc, sb_,
+                               batch > 1 ? sB : 0, batch > 1 ? sA : 0, batch > 1 ? sC : 0) == 0;
+    return vkblas_gemm_z64((vkblas_op_t)oa, (vkblas_op_t)ob, (uint32_t)n, (uint32_t)m, (uint32_t)k,
+                           a.x, a.y, B, (uint32_t)ldb, A, (uint32_t)lda, b.x, b.y, C,
+                           (uint32_t)ldc, sb_, batch > 1 ? sB : 0, batch > 1 ? sA : 0,
+                           batch > 1 ? sC : 0) == 0;
+}
+
+}  // namespace
 
 SHIM_EXPORT hipblasStatus_t hipblasDgemm(hipblasHandle_t handle, hipblasOperation_t transA,
                                          hipblasOperation_t transB, int m, int n, int k,
@@ -363,6 +447,9 @@ SHIM_EXPORT hipblasStatus_t hipblasDgemm(hipblasHandle_t handle, hipblasOperatio
                                          const double* BP, int ldb, const double* beta,
                                          double* CP, int ldc) {
     CHECK_MNK(m, n, k);
+    if (run_d(as_hip(handle), transA, transB, m, n, k, alpha, AP, lda, 0, BP, ldb, 0, beta, CP, ldc,
+              0, 1))
+        return HIPBLAS_STATUS_SUCCESS;
     return FWD_H(hipblasDgemm, handle, transA, transB, m, n, k, alpha, AP, lda, BP, ldb, beta, CP, ldc);
 }
 SHIM_EXPORT hipblasStatus_t hipblasDgemmStridedBatched(
@@ -372,6 +459,9 @@ SHIM_EXPORT hipblasStatus_t hipblasDgemmStridedBatched(
     int batchCount) {
     CHECK_MNK(m, n, k);
     if (batchCount <= 0) return HIPBLAS_STATUS_INVALID_VALUE;
+    if (run_d(as_hip(handle), transA, transB, m, n, k, alpha, AP, lda, strideA, BP, ldb, strideB,
+              beta, CP, ldc, strideC, batchCount))
+        return HIPBLAS_STATUS_SUCCESS;
     return FWD_H(hipblasDgemmStridedBatched, handle, transA, transB, m, n, k, alpha, AP, lda,
                  strideA, BP, ldb, strideB, beta, CP, ldc, strideC, batchCount);
 }
@@ -381,6 +471,9 @@ SHIM_EXPORT hipblasStatus_t hipblasCgemm_v2(hipblasHandle_t handle, hipblasOpera
                                             const hipComplex* BP, int ldb, const hipComplex* beta,
                                             hipComplex* CP, int ldc) {
     CHECK_MNK(m, n, k);
+    if (run_cx(as_hip(handle), transA, transB, m, n, k, alpha, AP, lda, 0, BP, ldb, 0, beta, CP,
+               ldc, 0, 1))
+        return HIPBLAS_STATUS_SUCCESS;
     return FWD_H(hipblasCgemm_v2, handle, transA, transB, m, n, k, alpha, AP, lda, BP, ldb, beta, CP, ldc);
 }
 SHIM_EXPORT hipblasStatus_t hipblasCgemmStridedBatched_v2(
@@ -390,6 +483,9 @@ SHIM_EXPORT hipblasStatus_t hipblasCgemmStridedBatched_v2(
     int ldc, long long strideC, int batchCount) {
     CHECK_MNK(m, n, k);
     if (batchCount <= 0) return HIPBLAS_STATUS_INVALID_VALUE;
+    if (run_cx(as_hip(handle), transA, transB, m, n, k, alpha, AP, lda, strideA, BP, ldb, strideB,
+               beta, CP, ldc, strideC, batchCount))
+        return HIPBLAS_STATUS_SUCCESS;
     return FWD_H(hipblasCgemmStridedBatched_v2, handle, transA, transB, m, n, k, alpha, AP, lda,
                  strideA, BP, ldb, strideB, beta, CP, ldc, strideC, batchCount);
 }
@@ -401,6 +497,9 @@ SHIM_EXPORT hipblasStatus_t hipblasZgemm_v2(hipblasHandle_t handle, hipblasOpera
                                             const hipDoubleComplex* beta, hipDoubleComplex* CP,
                                             int ldc) {
     CHECK_MNK(m, n, k);
+    if (run_cx(as_hip(handle), transA, transB, m, n, k, alpha, AP, lda, 0, BP, ldb, 0, beta, CP,
+               ldc, 0, 1))
+        return HIPBLAS_STATUS_SUCCESS;
     return FWD_H(hipblasZgemm_v2, handle, transA, transB, m, n, k, alpha, AP, lda, BP, ldb, beta, CP, ldc);
 }
 SHIM_EXPORT hipblasStatus_t hipblasZgemmStridedBatched_v2(
@@ -410,6 +509,9 @@ SHIM_EXPORT hipblasStatus_t hipblasZgemmStridedBatched_v2(
     hipDoubleComplex* CP, int ldc, long long strideC, int batchCount) {
     CHECK_MNK(m, n, k);
     if (batchCount <= 0) return HIPBLAS_STATUS_INVALID_VALUE;
+    if (run_cx(as_hip(handle), transA, transB, m, n, k, alpha, AP, lda, strideA, BP, ldb, strideB,
+               beta, CP, ldc, strideC, batchCount))
+        return HIPBLAS_STATUS_SUCCESS;
     return FWD_H(hipblasZgemmStridedBatched_v2, handle, transA, transB, m, n, k, alpha, AP, lda,
                  strideA, BP, ldb, strideB, beta, CP, ldc, strideC, batchCount);
 }

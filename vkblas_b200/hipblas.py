@@ -34,6 +34,14 @@ _SIGS = {
     "hipblasGemmEx": [vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, i32, i32, vp, vp, i32,
                       i32, i32, i32],
     "hipblasDgemm": [vp, i32, i32, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32],
+    "hipblasDgemmStridedBatched": [vp, i32, i32, i32, i32, i32, vp, vp, i32, i64, vp, i32, i64,
+                                   vp, vp, i32, i64, i32],
+    "hipblasCgemm_v2": [vp, i32, i32, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32],
+    "hipblasCgemmStridedBatched_v2": [vp, i32, i32, i32, i32, i32, vp, vp, i32, i64, vp, i32, i64,
+                                      vp, vp, i32, i64, i32],
+    "hipblasZgemm_v2": [vp, i32, i32, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32],
+    "hipblasZgemmStridedBatched_v2": [vp, i32, i32, i32, i32, i32, vp, vp, i32, i64, vp, i32, i64,
+                                      vp, vp, i32, i64, i32],
     "hipblasSdot": [vp, i32, vp, i32, vp, i32, vp],
     "rocblas_create_handle": [C.POINTER(vp)],
     "rocblas_destroy_handle": [vp],
