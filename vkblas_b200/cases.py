@@ -5,6 +5,7 @@
     python -m vkblas_b200.cases hgemm  [--n 4096] [--shape M,N,K]    # fp16 tcgen05, hipBLAS T/N
     python -m vkblas_b200.cases gemv   [--m 1] [--splitk 4]          # decode, K=4096, N=14336, M<=64
     python -m vkblas_b200.cases gemv32 [--m 1] [--trans t|n]         # fp32 decode, K=4096, N=14336
+    python -m vkblas_b200.cases dgemm|zgemm [--n 2048]               # fp64 / complex128 N/N
     python -m vkblas_b200.cases batched                              # 256 x 2048^3 fp16 N/N
 
 Inputs are device-resident and seeded; each iteration is one library call on
@@ -23,7 +24,8 @@ from vkblas_b200 import hipblas as hb
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["sgemm", "sgemm-simt", "hgemm", "gemv", "gemv32", "batched"])
+    ap.add_argument("case", choices=["sgemm", "sgemm-simt", "hgemm", "gemv", "gemv32", "batched",
+                                     "dgemm", "zgemm"])
     ap.add_argument("--trans", default="t", choices=["t", "n"],
                     help="gemv32: hipBLAS transA of the weights (t: N x K rows, n: K x N)")
     ap.add_argument("--n", type=int, default=4096)
@@ -98,6 +100,22 @@ def main(argv=None) -> int:
             return vk.lib.hipblasSgemm(h.h, tA, vk.HIPBLAS_OP_N, O, M, K, al,
                                        Ws[turn[0] % 4].data_ptr(), lda, X.data_ptr(), K, be,
                                        C.data_ptr(), O)
+    elif a.case in ("dgemm", "zgemm"):
+        cplx = a.case == "zgemm"
+        w = 2 if cplx else 1
+        A = torch.randn(w * M * K, device="cuda", generator=g, dtype=torch.float64)
+        B = torch.randn(w * K * N, device="cuda", generator=g, dtype=torch.float64)
+        C = torch.zeros(w * M * N, device="cuda", dtype=torch.float64)
+        vk.set_stream(s)
+        # useful FLOP: a complex multiply-add is 4 real ones
+        flop, nbytes = (8.0 if cplx else 2.0) * M * N * K, 0.0
+        if cplx:
+            call = lambda: vk.lib.vkblas_gemm_z64(0, 0, M, N, K, 1.0, 0.0, A.data_ptr(), K,  # noqa: E731
+                                                  B.data_ptr(), N, 0.0, 0.0, C.data_ptr(), N, 1,
+                                                  0, 0, 0)
+        else:
+            call = lambda: vk.lib.vkblas_gemm_f64(0, 0, M, N, K, 1.0, A.data_ptr(), K,  # noqa: E731
+                                                  B.data_ptr(), N, 0.0, C.data_ptr(), N, 1, 0, 0, 0)
     else:
         b, n = 256, 2048
         A = (torch.randn(b * n * n, device="cuda", generator=g) * 0.02).half()
