@@ -84,7 +84,7 @@ cudaError_t launch_gemv_f32(const GemmProblem& p, int splitk, void* workspace, c
 bool umma_supported(const GemmProblem& p);
 bool umma_profitable(const GemmProblem& p);
 size_t umma_workspace_bytes(const GemmProblem& p);
-// Split-K / stream-K tail scratch: [tickets (zero, left zero)][partials]; 0 = no split.
+// Split-K / wave-tail scratch: fp32 partial tiles of the split units; 0 = no split.
 size_t umma_split_workspace_bytes(const GemmProblem& p, int num_sms);
 int umma_split_count(const GemmProblem& p, int num_sms);   // K splits of the last wave (1 = none)
 // True when the call runs on 2-CTA clusters (256-row tiles, cta_group::2).
