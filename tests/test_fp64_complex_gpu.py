@@ -84,6 +84,23 @@ def test_f64_batched(bcast, cuda):
     assert np.array_equal(dC.cpu().numpy().view(np.uint64), want.view(np.uint64))
 
 
+def test_f64_batch_above_grid_z_limit(cuda):
+    """More batch entries than a grid's z extent (65535): the kernel strides over them."""
+    import torch
+    M, N, K, batch = 3, 2, 5, 70000
+    lda, ldb, ldc, sa, sb, sc, na, nb, nc = _layout(0, 0, M, N, K, batch)
+    rng = np.random.default_rng(11)
+    A, B, C0 = rng.standard_normal(na), rng.standard_normal(nb), rng.standard_normal(nc)
+    dA, dB, dC = _dev(A), _dev(B), _dev(C0)
+    _sync_stream()
+    assert vk.lib.vkblas_gemm_f64(0, 0, M, N, K, 1.25, dA.data_ptr(), lda, dB.data_ptr(), ldb, 0.5,
+                                  dC.data_ptr(), ldc, batch, sa, sb, sc) == 0
+    torch.cuda.synchronize()
+    want = C0.copy()
+    orc.dgemm_rowmajor_seq(0, 0, M, N, K, 1.25, A, lda, B, ldb, 0.5, want, ldc, batch, sa, sb, sc)
+    assert np.array_equal(dC.cpu().numpy().view(np.uint64), want.view(np.uint64))
+
+
 def _cx(rng, n, dt):
     return rng.standard_normal(2 * n).astype(dt)        # interleaved re, im
 
@@ -131,6 +148,17 @@ def test_c64_exact_path_bit_exact(ops, shape, cuda):
 def test_complex_batched_beta_zero(bcast, cuda):
     got, want, _, _ = _run_cx(True, (1, 0), 48, 40, 64, 1.0 + 1.0j, 0j, batch=3, bcast=bcast)
     assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
+
+
+@pytest.mark.parametrize("bcast", [None, "b"])
+def test_complex_batch_above_grid_z_limit(bcast, cuda):
+    """70000 batch entries: the planar split, the real GEMMs and the combine all stride in z."""
+    got, want, _, _ = _run_cx(True, (0, 1), 2, 3, 4, 0.5 - 1.0j, 0.25 + 0.5j, batch=70000,
+                              bcast=bcast)
+    assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
+    got, want, _, _ = _run_cx(False, (1, 0), 2, 3, 4, 0.5 - 1.0j, 0.25 + 0.5j, batch=70000,
+                              bcast=bcast, path=vk.PATH_SIMT)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
 def test_c64_default_path_accuracy(cuda):

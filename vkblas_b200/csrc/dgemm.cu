@@ -31,6 +31,7 @@ struct DArgs {
     const double* B; uint32_t ldb;
     double* C; uint32_t ldc;
     int64_t sa, sb, sc;
+    uint32_t batch;
 };
 
 // Thread (tx, ty) of a 16 x 16 layout owns rows ty + 16 i and columns
@@ -40,7 +41,8 @@ __global__ void __launch_bounds__(DTHREADS) dgemm_kernel(DArgs a) {
     __shared__ double As[DBK][DT + 1];     // [k][m]
     __shared__ double Bs[DBK][DT + 1];     // [k][n]
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const uint32_t b = blockIdx.z, m0 = blockIdx.y * DT, n0 = blockIdx.x * DT;
+    const uint32_t m0 = blockIdx.y * DT, n0 = blockIdx.x * DT;
+    for (uint32_t b = blockIdx.z; b < a.batch; b += gridDim.z) {
     const double* A = a.A + a.sa * (int64_t)b;
     const double* B = a.B + a.sb * (int64_t)b;
     double acc[4][4];
@@ -96,21 +98,23 @@ __global__ void __launch_bounds__(DTHREADS) dgemm_kernel(DArgs a) {
             *c = __dadd_rn(__dmul_rn(a.alpha, acc[i][j]), __dmul_rn(a.beta, old));
         }
     }
+    }   // batch entries, striding by gridDim.z
 }
 
 // Interleaved complex [b*stride + r*ld + c] -> real and imaginary planes at
 // the same element offsets, for r < rows, c < cols.
 template <typename T>
 __global__ void cx_split_kernel(const T* __restrict__ src, uint32_t rows, uint32_t cols,
-                                uint32_t ld, int64_t stride, T* __restrict__ re,
+                                uint32_t ld, int64_t stride, uint32_t batch, T* __restrict__ re,
                                 T* __restrict__ im) {
     const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= cols) return;
-    for (uint32_t r = blockIdx.y; r < rows; r += gridDim.y) {
-        const size_t o = (size_t)(stride * (int64_t)blockIdx.z) + (size_t)r * ld + c;
-        re[o] = src[2 * o];
-        im[o] = src[2 * o + 1];
-    }
+    for (uint32_t b = blockIdx.z; b < batch; b += gridDim.z)
+        for (uint32_t r = blockIdx.y; r < rows; r += gridDim.y) {
+            const size_t o = (size_t)(stride * (int64_t)b) + (size_t)r * ld + c;
+            re[o] = src[2 * o];
+            im[o] = src[2 * o + 1];
+        }
 }
 
 __device__ __forceinline__ float mul_rn(float x, float y) { return __fmul_rn(x, y); }
@@ -123,12 +127,13 @@ __device__ __forceinline__ double sub_rn(double x, double y) { return __dsub_rn(
 // C = alpha * (T1 + i T2) + beta * C over M x N per batch entry (C interleaved).
 template <typename T>
 __global__ void cx_combine_kernel(const T* __restrict__ t1, const T* __restrict__ t2, T* C,
-                                  uint32_t M, uint32_t N, uint32_t ldc, int64_t sc, T ar, T ai,
-                                  T br, T bi) {
+                                  uint32_t M, uint32_t N, uint32_t ldc, int64_t sc, uint32_t batch,
+                                  T ar, T ai, T br, T bi) {
     const uint32_t n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= N) return;
+    for (uint32_t b = blockIdx.z; b < batch; b += gridDim.z)
     for (uint32_t m = blockIdx.y; m < M; m += gridDim.y) {
-        const size_t o = (size_t)(sc * (int64_t)blockIdx.z) + (size_t)m * ldc + n;
+        const size_t o = (size_t)(sc * (int64_t)b) + (size_t)m * ldc + n;
         const T fr = t1[o], fi = t2[o];
         T outr = sub_rn(mul_rn(ar, fr), mul_rn(ai, fi));
         T outi = add_rn(mul_rn(ar, fi), mul_rn(ai, fr));
@@ -148,9 +153,9 @@ cudaError_t launch_dgemm(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K,
                          const double* A, uint32_t lda, const double* B, uint32_t ldb, double beta,
                          double* C, uint32_t ldc, uint32_t batch, int64_t sa, int64_t sb,
                          int64_t sc, cudaStream_t s) {
-    DArgs a{op_a, op_b, M, N, K, alpha, beta, A, lda, B, ldb, C, ldc, sa, sb, sc};
-    const dim3 grid((N + DT - 1) / DT, (M + DT - 1) / DT, batch);
-    if (grid.y > 65535 || grid.z > 65535) return cudaErrorInvalidConfiguration;
+    DArgs a{op_a, op_b, M, N, K, alpha, beta, A, lda, B, ldb, C, ldc, sa, sb, sc, batch};
+    const dim3 grid((N + DT - 1) / DT, (M + DT - 1) / DT, batch < 65535u ? batch : 65535u);
+    if (grid.y > 65535) return cudaErrorInvalidConfiguration;
     dgemm_kernel<<<grid, DTHREADS, 0, s>>>(a);
     count_launch();
     return cudaGetLastError();
@@ -158,15 +163,15 @@ cudaError_t launch_dgemm(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K,
 
 cudaError_t launch_cx_split(bool dbl, const void* src, uint32_t rows, uint32_t cols, uint32_t ld,
                             int64_t stride, uint32_t batch, void* re, void* im, cudaStream_t s) {
-    const dim3 grid((cols + 255) / 256, rows < 65535u ? rows : 65535u, stride ? batch : 1);
-    if (grid.z > 65535) return cudaErrorInvalidConfiguration;
+    const uint32_t nb = stride ? batch : 1u;        // a broadcast operand is split once
+    const dim3 grid((cols + 255) / 256, rows < 65535u ? rows : 65535u, nb < 65535u ? nb : 65535u);
     if (dbl)
         cx_split_kernel<double><<<grid, 256, 0, s>>>(static_cast<const double*>(src), rows, cols,
-                                                       ld, stride, static_cast<double*>(re),
+                                                       ld, stride, nb, static_cast<double*>(re),
                                                        static_cast<double*>(im));
     else
         cx_split_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(src), rows, cols, ld,
-                                                      stride, static_cast<float*>(re),
+                                                      stride, nb, static_cast<float*>(re),
                                                       static_cast<float*>(im));
     count_launch();
     return cudaGetLastError();
@@ -175,16 +180,15 @@ cudaError_t launch_cx_split(bool dbl, const void* src, uint32_t rows, uint32_t c
 cudaError_t launch_cx_combine(bool dbl, const void* t1, const void* t2, void* C, uint32_t M,
                               uint32_t N, uint32_t ldc, int64_t sc, uint32_t batch, double ar,
                               double ai, double br, double bi, cudaStream_t s) {
-    const dim3 grid((N + 255) / 256, M < 65535u ? M : 65535u, batch);
-    if (grid.z > 65535) return cudaErrorInvalidConfiguration;
+    const dim3 grid((N + 255) / 256, M < 65535u ? M : 65535u, batch < 65535u ? batch : 65535u);
     if (dbl)
         cx_combine_kernel<double><<<grid, 256, 0, s>>>(
             static_cast<const double*>(t1), static_cast<const double*>(t2), static_cast<double*>(C),
-            M, N, ldc, sc, ar, ai, br, bi);
+            M, N, ldc, sc, batch, ar, ai, br, bi);
     else
         cx_combine_kernel<float><<<grid, 256, 0, s>>>(
             static_cast<const float*>(t1), static_cast<const float*>(t2), static_cast<float*>(C), M,
-            N, ldc, sc, (float)ar, (float)ai, (float)br, (float)bi);
+            N, ldc, sc, batch, (float)ar, (float)ai, (float)br, (float)bi);
     count_launch();
     return cudaGetLastError();
 }
