@@ -75,6 +75,9 @@ struct __align__(64) UmmaParams {
     // shapes, weight rows on the MMA's 128 lanes) and element (row, col) of
     // its tile goes to C + col * ldc + row.
     uint32_t c_trans;
+    // k-block order rotation (small-M tiles only): a unit of tile t starts its
+    // k range at (t * k_rot_mul) % len and wraps around (0 = plain order).
+    uint32_t k_rot_mul;
     uint64_t wait_limit_ns;      // bound of every mbarrier wait
     uint32_t test_skip_first_load;   // test hook: the first stage is never filled
 };
@@ -307,14 +310,21 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                 const int32_t m0 = (int32_t)(mb * C_::BM_TILE + rank * BM);
                 const int32_t n0 = (int32_t)(nb * BN + rank * C_::BNC);
                 const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
-                for (uint32_t kb = ukb0; kb < ukb1; kb++) {
+                const uint32_t len = ukb1 - ukb0;
+                // Only the weight-streaming small-M tiles (BN = 64) rotate: all
+                // tiles start together, and in plain order every weight row
+                // would be read at the same k offset at the same time, which
+                // loads the HBM channels unevenly.
+                const uint32_t rot = (BN == 64 && p.k_rot_mul) ? (t * p.k_rot_mul) % len : 0u;
+                for (uint32_t i = 0; i < len; i++) {
+                    const uint32_t kb = ukb0 + (i + rot < len ? i + rot : i + rot - len);
                     if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
                                   DS_TIMEOUT_PRODUCER, p.wait_limit_ns)) {
                         ok = false;
                         break;
                     }
                     const uint32_t fb = to_issuer(full_bar(stage));
-                    if (p.test_skip_first_load && u == unit0 && kb == ukb0) {
+                    if (p.test_skip_first_load && u == unit0 && i == 0) {
                         // Test hook: leave this stage empty so its consumer's
                         // bounded wait runs out (no copy is issued).
                         if (++stage == STAGES) {
@@ -917,6 +927,7 @@ bool pair_enabled() {
 // Small-M 2-byte GEMMs (decode with up to 64 tokens) run transposed: weight
 // rows on the MMA's 128 lanes, tokens on a 64-wide N tile, an 8-deep ring.
 constexpr int BN_SM = 64, STAGES_SM = 8;
+constexpr uint32_t K_ROT_MUL = 29;
 constexpr uint32_t SMALL_M_MAX = 64;
 
 bool small_m_swap(const GemmProblem& p) {
@@ -1064,6 +1075,12 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     const KernelShape ks = kernel_shape(p_in);
     const GemmProblem& p = ks.q;                 // the (possibly transposed) problem run
     prm.c_trans = ks.c_trans ? 1u : 0u;
+    // Rotated k order for the weight-streaming tiles.  Measured on B200 at
+    // 4096 -> 14336, M = 16-64: multiplier 29 took 24.9-26.7 us to
+    // 23.5-25.3 us; 7 gained less; 1 (neighbouring tiles one k-block apart)
+    // lost 1 us.  Large tiles keep the plain order, because neighbouring
+    // tiles there share A and B k-blocks in L2.
+    prm.k_rot_mul = ks.c_trans ? K_ROT_MUL : 0u;
     const Operand a = operand_a(p), b = operand_b(p);
     const bool is32 = p.dtype == DT_F32;
     const int BN = (int)ks.BN;
