@@ -167,6 +167,30 @@ def secondary_results(vk, hb, torch, peaks):
     g = torch.Generator(device="cuda").manual_seed(3)
     with hb.Handle() as h, torch.cuda.stream(s):
         h.set_stream(s)
+        # config 2, second kernel: the exact FFMA SIMT SGEMM at 4096^3 NN (two
+        # input sets of 128 MiB, larger than L2, alternated call by call)
+        n = 4096
+        sets = [(torch.randn(n * n, device="cuda", generator=g),
+                 torch.randn(n * n, device="cuda", generator=g),
+                 torch.empty(n * n, device="cuda")) for _ in range(2)]
+
+        def run_ffma(i):
+            A, B, C = sets[i % 2]
+            vk.lib.hipblasSgemm(h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, n, n, n, al, A.data_ptr(),
+                                n, B.data_ptr(), n, be, C.data_ptr(), n)
+        vk.set_path(vk.PATH_SIMT)
+        try:
+            for i in range(3):
+                run_ffma(i)
+            ms = _time_loop(run_ffma, 6, s)
+            path = vk.PATH_NAMES[vk.last_path()]
+        finally:
+            vk.set_path(vk.PATH_AUTO)
+        tf = 2.0 * n ** 3 / ms / 1e9
+        nominal = 148 * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+        out["sgemm_ffma_nn_4096"] = {"tflops": round(tf, 2), "ms": round(ms, 4), "path": path,
+                                     "frac_of_fp32_nominal": round(tf / nominal, 4)}
+        del sets
         # config 3: HGEMM T/N 4096^3, 8192^3 and 16384^3
         for n in (4096, 8192, 16384):
             sets = [((torch.randn(n, n, device="cuda", generator=g) * 0.02).half(),
