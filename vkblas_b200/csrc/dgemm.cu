@@ -21,7 +21,16 @@
 namespace vkb {
 namespace {
 
-constexpr int DT = 64, DBK = 8, DTHREADS = 256;   // 64x64 tile, 4x4 outputs per thread
+// 64 x 128 CTA tile, 128 threads, 8 x 8 outputs per thread: rows ty*2 + i +
+// 16*g (i < 2, g < 4), columns tx*2 + j + 32*h (j < 2, h < 4).  A k step reads
+// eight 128-bit fragments (two doubles each) from k-major shared tiles for 64
+// FMAs -- half the shared-memory traffic per FMA of a 4 x 4 tile, which kept
+// the FP64 pipe at about 40% -- and the next step's fragments are read while
+// the current step's FMAs issue.  Fragment reads are conflict-free: 16 lanes
+// cover 256 contiguous bytes of a B row, and the A reads of a warp are two
+// broadcasts.  Global k-tiles arrive by cp.async into two shared stages (no
+// registers held), so tile k + 1 lands while tile k is multiplied.
+constexpr int DBM = 64, DBN = 128, DBK = 8, DTHREADS = 128;
 
 struct DArgs {
     int op_a, op_b;
@@ -34,64 +43,111 @@ struct DArgs {
     uint32_t batch;
 };
 
-// Thread (tx, ty) of a 16 x 16 layout owns rows ty + 16 i and columns
-// tx + 16 j of the tile: shared-memory reads are consecutive doubles across
-// the warp and C stores are coalesced along n.
+// 8-byte asynchronous copy global -> shared; `valid` false writes zero and
+// reads nothing.
+__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool valid) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src),
+                 "r"(valid ? 8 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One k-tile of an operand (R rows/columns x 8 k) -> shared memory S[k][r],
+// R * 8 / 128 elements per thread, in an order that keeps global loads
+// coalesced: along k for a k-contiguous operand, along r otherwise.
+template <int R>
+__device__ __forceinline__ void load_dtile(const double* X, bool k_contig, uint32_t ld,
+                                           uint32_t rows, uint32_t K, uint32_t r0, uint32_t k0,
+                                           int tid, double (*S)[R + 2]) {
+    constexpr int PER = R * DBK / DTHREADS;
+#pragma unroll
+    for (int q = 0; q < PER; q++) {
+        const int e = q * DTHREADS + tid;
+        int r, k;
+        if (k_contig) { r = e >> 3; k = e & 7; }      // X[r*ld + k]
+        else { k = e / R; r = e % R; }                // X[k*ld + r]
+        const uint32_t gr = r0 + r, gk = k0 + k;
+        const bool in = gr < rows && gk < K;
+        const double* src = in ? (k_contig ? X + (size_t)gr * ld + gk : X + (size_t)gk * ld + gr) : X;
+        cp_async8(&S[k][r], src, in);
+    }
+}
+
 __global__ void __launch_bounds__(DTHREADS) dgemm_kernel(DArgs a) {
-    __shared__ double As[DBK][DT + 1];     // [k][m]
-    __shared__ double Bs[DBK][DT + 1];     // [k][n]
+    __shared__ __align__(16) double As[2][DBK][DBM + 2];  // [stage][k][m]
+    __shared__ __align__(16) double Bs[2][DBK][DBN + 2];  // [stage][k][n]
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const uint32_t m0 = blockIdx.y * DT, n0 = blockIdx.x * DT;
+    const uint32_t m0 = blockIdx.y * DBM, n0 = blockIdx.x * DBN;
+    const bool a_kc = a.op_a == 0, b_kc = a.op_b != 0;
     for (uint32_t b = blockIdx.z; b < a.batch; b += gridDim.z) {
     const double* A = a.A + a.sa * (int64_t)b;
     const double* B = a.B + a.sb * (int64_t)b;
-    double acc[4][4];
+    double acc[8][8];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 8; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
-    for (uint32_t k0 = 0; k0 < a.K; k0 += DBK) {
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int e = tid * 2 + h;                     // 512 elements per operand tile
-            uint32_t m, k;
-            if (a.op_a == 0) { m = e >> 3; k = e & 7; }     // A[m*lda + k]: along k
-            else { k = e >> 6; m = e & 63; }                // A[k*lda + m]: along m
-            const uint32_t gm = m0 + m, gk = k0 + k;
-            As[k][m] = (gm < a.M && gk < a.K)
-                           ? (a.op_a == 0 ? A[(size_t)gm * a.lda + gk] : A[(size_t)gk * a.lda + gm])
-                           : 0.0;
-            uint32_t n, kb;
-            if (a.op_b == 0) { kb = e >> 6; n = e & 63; }   // B[k*ldb + n]: along n
-            else { n = e >> 3; kb = e & 7; }                // B[n*ldb + k]: along k
-            const uint32_t gn = n0 + n, gkb = k0 + kb;
-            Bs[kb][n] = (gn < a.N && gkb < a.K)
-                            ? (a.op_b == 0 ? B[(size_t)gkb * a.ldb + gn] : B[(size_t)gn * a.ldb + gkb])
-                            : 0.0;
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+    const uint32_t ktiles = (a.K + DBK - 1) / DBK;
+    load_dtile<DBM>(A, a_kc, a.lda, a.M, a.K, m0, 0, tid, As[0]);
+    load_dtile<DBN>(B, b_kc, a.ldb, a.N, a.K, n0, 0, tid, Bs[0]);
+    cp_async_commit();
+    for (uint32_t kt = 0; kt < ktiles; kt++) {
+        const uint32_t k0 = kt * DBK;
+        const int st = kt & 1;
+        if (kt + 1 < ktiles) {             // next tile into the other stage
+            load_dtile<DBM>(A, a_kc, a.lda, a.M, a.K, m0, k0 + DBK, tid, As[st ^ 1]);
+            load_dtile<DBN>(B, b_kc, a.ldb, a.N, a.K, n0, k0 + DBK, tid, Bs[st ^ 1]);
+            cp_async_commit();
+            cp_async_wait<1>();            // this tile's group has landed
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
         const uint32_t kend = min((uint32_t)DBK, a.K - k0);   // stop at K: no extra terms
-        for (uint32_t kk = 0; kk < kend; kk++) {
-            double av[4], bv[4];
+        double2 fa[2][4], fb[2][4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) av[i] = As[kk][ty + 16 * i];
-#pragma unroll
-            for (int j = 0; j < 4; j++) bv[j] = Bs[kk][tx + 16 * j];
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] = __fma_rn(av[i], bv[j], acc[i][j]);
+        for (int g = 0; g < 4; g++) {
+            fa[0][g] = *reinterpret_cast<const double2*>(&As[st][0][ty * 2 + 16 * g]);
+            fb[0][g] = *reinterpret_cast<const double2*>(&Bs[st][0][tx * 2 + 32 * g]);
         }
-        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < DBK; kk++) {
+            if ((uint32_t)kk < kend) {
+                const int c = kk & 1;
+                if (kk + 1 < DBK) {
+#pragma unroll
+                    for (int g = 0; g < 4; g++) {
+                        fa[c ^ 1][g] = *reinterpret_cast<const double2*>(&As[st][kk + 1][ty * 2 + 16 * g]);
+                        fb[c ^ 1][g] = *reinterpret_cast<const double2*>(&Bs[st][kk + 1][tx * 2 + 32 * g]);
+                    }
+                }
+#pragma unroll
+                for (int g = 0; g < 4; g++)
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        acc[2 * g][2 * h] = __fma_rn(fa[c][g].x, fb[c][h].x, acc[2 * g][2 * h]);
+                        acc[2 * g][2 * h + 1] = __fma_rn(fa[c][g].x, fb[c][h].y, acc[2 * g][2 * h + 1]);
+                        acc[2 * g + 1][2 * h] = __fma_rn(fa[c][g].y, fb[c][h].x, acc[2 * g + 1][2 * h]);
+                        acc[2 * g + 1][2 * h + 1] = __fma_rn(fa[c][g].y, fb[c][h].y, acc[2 * g + 1][2 * h + 1]);
+                    }
+            }
+        }
+        __syncthreads();                   // stage st is refilled two tiles on
     }
     double* C = a.C + a.sc * (int64_t)b;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint32_t m = m0 + ty + 16 * i;
+    for (int i = 0; i < 8; i++) {
+        const uint32_t m = m0 + ty * 2 + (i & 1) + 16 * (i >> 1);
         if (m >= a.M) continue;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const uint32_t n = n0 + tx + 16 * j;
+        for (int j = 0; j < 8; j++) {
+            const uint32_t n = n0 + tx * 2 + (j & 1) + 32 * (j >> 1);
             if (n >= a.N) continue;
             double* c = C + (size_t)m * a.ldc + n;
             const double old = (a.beta != 0.0) ? *c : 0.0;
@@ -154,7 +210,7 @@ cudaError_t launch_dgemm(int op_a, int op_b, uint32_t M, uint32_t N, uint32_t K,
                          double* C, uint32_t ldc, uint32_t batch, int64_t sa, int64_t sb,
                          int64_t sc, cudaStream_t s) {
     DArgs a{op_a, op_b, M, N, K, alpha, beta, A, lda, B, ldb, C, ldc, sa, sb, sc, batch};
-    const dim3 grid((N + DT - 1) / DT, (M + DT - 1) / DT, batch < 65535u ? batch : 65535u);
+    const dim3 grid((N + DBN - 1) / DBN, (M + DBM - 1) / DBM, batch < 65535u ? batch : 65535u);
     if (grid.y > 65535) return cudaErrorInvalidConfiguration;
     dgemm_kernel<<<grid, DTHREADS, 0, s>>>(a);
     count_launch();
