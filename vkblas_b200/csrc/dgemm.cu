@@ -24,9 +24,8 @@ namespace {
 // 64 x 128 CTA tile, 128 threads, 8 x 8 outputs per thread: rows ty*2 + i +
 // 16*g (i < 2, g < 4), columns tx*2 + j + 32*h (j < 2, h < 4).  A k step reads
 // eight 128-bit fragments (two doubles each) from k-major shared tiles for 64
-// FMAs -- half the shared-memory traffic per FMA of a 4 x 4 tile, which kept
-// the FP64 pipe at about 40% -- and the next step's fragments are read while
-// the current step's FMAs issue.  Fragment reads are conflict-free: 16 lanes
+// FMAs, half the shared-memory traffic per FMA of a 4 x 4 tile.  Fragment
+// reads are conflict-free: 16 lanes
 // cover 256 contiguous bytes of a B row, and the A reads of a warp are two
 // broadcasts.  Global k-tiles arrive by cp.async into two shared stages (no
 // registers held), so tile k + 1 lands while tile k is multiplied.
@@ -110,31 +109,23 @@ __global__ void __launch_bounds__(DTHREADS) dgemm_kernel(DArgs a) {
         }
         __syncthreads();
         const uint32_t kend = min((uint32_t)DBK, a.K - k0);   // stop at K: no extra terms
-        double2 fa[2][4], fb[2][4];
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            fa[0][g] = *reinterpret_cast<const double2*>(&As[st][0][ty * 2 + 16 * g]);
-            fb[0][g] = *reinterpret_cast<const double2*>(&Bs[st][0][tx * 2 + 32 * g]);
-        }
 #pragma unroll
         for (int kk = 0; kk < DBK; kk++) {
             if ((uint32_t)kk < kend) {
-                const int c = kk & 1;
-                if (kk + 1 < DBK) {
+                double2 fa[4], fb[4];
 #pragma unroll
-                    for (int g = 0; g < 4; g++) {
-                        fa[c ^ 1][g] = *reinterpret_cast<const double2*>(&As[st][kk + 1][ty * 2 + 16 * g]);
-                        fb[c ^ 1][g] = *reinterpret_cast<const double2*>(&Bs[st][kk + 1][tx * 2 + 32 * g]);
-                    }
+                for (int g = 0; g < 4; g++) {
+                    fa[g] = *reinterpret_cast<const double2*>(&As[st][kk][ty * 2 + 16 * g]);
+                    fb[g] = *reinterpret_cast<const double2*>(&Bs[st][kk][tx * 2 + 32 * g]);
                 }
 #pragma unroll
                 for (int g = 0; g < 4; g++)
 #pragma unroll
                     for (int h = 0; h < 4; h++) {
-                        acc[2 * g][2 * h] = __fma_rn(fa[c][g].x, fb[c][h].x, acc[2 * g][2 * h]);
-                        acc[2 * g][2 * h + 1] = __fma_rn(fa[c][g].x, fb[c][h].y, acc[2 * g][2 * h + 1]);
-                        acc[2 * g + 1][2 * h] = __fma_rn(fa[c][g].y, fb[c][h].x, acc[2 * g + 1][2 * h]);
-                        acc[2 * g + 1][2 * h + 1] = __fma_rn(fa[c][g].y, fb[c][h].y, acc[2 * g + 1][2 * h + 1]);
+                        acc[2 * g][2 * h] = __fma_rn(fa[g].x, fb[h].x, acc[2 * g][2 * h]);
+                        acc[2 * g][2 * h + 1] = __fma_rn(fa[g].x, fb[h].y, acc[2 * g][2 * h + 1]);
+                        acc[2 * g + 1][2 * h] = __fma_rn(fa[g].y, fb[h].x, acc[2 * g + 1][2 * h]);
+                        acc[2 * g + 1][2 * h + 1] = __fma_rn(fa[g].y, fb[h].y, acc[2 * g + 1][2 * h + 1]);
                     }
             }
         }
