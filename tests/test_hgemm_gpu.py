@@ -218,6 +218,44 @@ def test_gemv_edges_against_splitk_oracle(dt, shape, splitk, cuda):
     assert np.max(np.abs(got - orc.widen(dt, ref).reshape(M, N))) <= 0.02
 
 
+def _auto_gemv_split(M, N, K, sms):
+    """The GEMV's automatic split-K rule: about 24 resident warps per SM (CTAs of 8
+    warps, 4 when M > 8), and for 4-warp CTAs a grid within one wave of 8 per SM."""
+    two = M > 8
+    kw = 4 if two else 8
+    ctas = (N + 15) // 16
+    s = 1
+    while (s < 16 and ctas * s < (24 // kw) * sms and K // (2 * s) >= kw * 128
+           and (not two or ctas * 2 * s <= 8 * sms)):
+        s *= 2
+    return s
+
+
+@pytest.mark.parametrize("shape", [(12, 4096, 14336), (16, 1024, 4096), (9, 11008, 1024),
+                                   (4, 4096, 14336), (16, 300, 2048)])
+def test_gemv_auto_split(shape, cuda):
+    """Automatic split-K factors (M > 8 uses 4-warp CTAs) against the fp64 oracle."""
+    import torch
+    M, N, K = shape
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    rng = np.random.default_rng(M * 7 + N + K)
+    X = orc.narrow(0, rng.uniform(-1, 1, M * K).astype(np.float32))
+    W = orc.narrow(0, (rng.uniform(-1, 1, N * K) * 0.05).astype(np.float32))
+    C0 = orc.narrow(0, rng.uniform(-1, 1, M * N).astype(np.float32))
+    dX, dW, dC = dev_u16(X, 0), dev_u16(W, 0), dev_u16(C0, 0)
+    vk.set_stream(torch.cuda.current_stream())
+    st = vk.gemm(vk.DT_F16, 0, 1, M, N, K, 1.0, dX.data_ptr(), K, dW.data_ptr(), K, 0.5,
+                 dC.data_ptr(), N)
+    torch.cuda.synchronize()
+    assert st == vk.VKBLAS_OK
+    assert vk.last_path() == vk.PATH_GEMV
+    assert vk.last_split() == _auto_gemv_split(M, N, K, sms)
+    check_status()
+    want = orc.hgemm_rowmajor_f64(0, 0, 1, M, N, K, 1.0, X, K, W, K, 0.5, C0, N)[0]
+    got = orc.widen(0, host_u16(dC)).reshape(M, N)
+    assert orc.rel_frobenius(got, want) <= 2e-3
+
+
 def test_config5_strided_batched_hgemm(cuda):
     """256 x 2048^3 fp16 NN strided-batched, sampled check."""
     import torch
