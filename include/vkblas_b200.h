@@ -35,6 +35,17 @@ vkblas_status_t vkblas_gemm_ex(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op
                                int64_t stride_a, int64_t stride_b, int64_t stride_c,
                                void* stream);
 
+/* Frees this library's scratch workspaces on the current device: the ones
+ * bound to `stream` (a cudaStream_t; NULL = legacy default stream) when
+ * all == 0, or every stream's when all != 0.  Workspaces are grow-only and
+ * kept per (device, stream) -- the 3xTF32 operand planes of a 4096^3 SGEMM
+ * take 256 MB -- so a caller that ran GEMMs on many streams, or on a stream it
+ * has destroyed, calls this to give the memory back; the next call that needs
+ * scratch allocates it again.  Synchronises the device first.  Must not run
+ * while another thread issues calls on this device.  Returns 0, or -1 when
+ * no CUDA device state is available.  No counterpart in the reference. */
+int vkblas_b200_release_workspaces(void* stream, int all);
+
 /* Split-K decode GEMV that allocates nothing.  No counterpart in the
  * reference.  For callers that cannot let a library call cudaMalloc (work
  * inside a framework's allocator or memory pool, or decode loops where a

@@ -76,6 +76,8 @@ def _load() -> C.CDLL:
     lib.vkblas_b200_device_status.argtypes = [i32]
     lib.vkblas_b200_device_status.restype = i32
     lib.vkblas_b200_launch_count.restype = C.c_uint64
+    lib.vkblas_b200_release_workspaces.argtypes = [vp, i32]
+    lib.vkblas_b200_release_workspaces.restype = i32
     lib.vkblas_b200_version.restype = C.c_char_p
     lib.vkblas_cache_invalidate_base.argtypes = [vp]
     lib.vkblas_shard_range.argtypes = [C.c_uint64, C.c_uint64, i32, i32,
@@ -136,6 +138,15 @@ def set_splitk(s: int) -> None:
 
 def device_status(clear: bool = True) -> int:
     return _get().vkblas_b200_device_status(1 if clear else 0)
+
+
+def release_workspaces(stream=None, all_streams: bool = False) -> None:
+    """Free the library's scratch for `stream` (a torch.cuda.Stream, a raw
+    handle or None = default stream), or for every stream; synchronises the device."""
+    if stream is not None and hasattr(stream, "cuda_stream"):
+        stream = stream.cuda_stream
+    if _get().vkblas_b200_release_workspaces(stream, 1 if all_streams else 0) != 0:
+        raise VkblasError("vkblas_b200_release_workspaces failed")
 
 
 def launch_count() -> int:

@@ -501,6 +501,34 @@ VKB_EXPORT int vkblas_b200_device_status(int clear) {
     return v;
 }
 
+VKB_EXPORT int vkblas_b200_release_workspaces(void* stream, int all) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    DeviceState* ds = device_state(dev);
+    if (!ds) return -1;
+    // Queued kernels may still use the buffers.
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    std::lock_guard<std::mutex> lk(ds->mu);
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    for (auto& kind : ds->ws) {
+        for (auto it = kind.begin(); it != kind.end();) {
+            if (all || it->first == s) {
+                if (it->second.ptr) cudaFree(it->second.ptr);
+                it = kind.erase(it);
+            } else {
+                ++it;
+            }
+        }
+    }
+    return 0;
+}
+
 VKB_EXPORT uint64_t vkblas_b200_launch_count(void) { return g_launches.load(); }
 
 VKB_EXPORT const char* vkblas_b200_version(void) { return "vkblas-b200 0.1 (sm_100a)"; }
