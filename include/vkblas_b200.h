@@ -89,6 +89,14 @@ int vkblas_b200_last_pair(void);
 /* Thread-local split-K factor for the GEMV path: 0 = automatic, else 1..16. */
 void vkblas_b200_set_splitk(int splitk);
 
+/* Measurement hook (thread-local; NULL, NULL turns it off): while set, each
+ * GEMM call made from this thread records the cudaEvent_t `start` on its
+ * stream right before its main kernel (after the 3xTF32 split pre-pass, when
+ * there is one) and `end` right after it (after the split-K reduce, when
+ * there is one).  Timing those events gives the kernel's own duration inside
+ * a stream of calls.  Both events must belong to the call's device. */
+void vkblas_b200_set_kernel_events(void* start, void* end);
+
 /* Device status word written by kernels whose bounded waits ran out (0 = no
  * error).  Synchronises the current device first.  clear != 0 resets it. */
 int vkblas_b200_device_status(int clear);

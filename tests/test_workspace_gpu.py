@@ -1,5 +1,7 @@
-"""Per-stream scratch workspaces: vkblas_b200_release_workspaces gives the
-memory back, and the next call on that stream allocates it again."""
+"""Engine housekeeping on a GPU: per-stream scratch workspaces
+(vkblas_b200_release_workspaces gives the memory back, and the next call on
+that stream allocates it again) and the kernel-timing event hook
+(vkblas_b200_set_kernel_events brackets a call's main kernel)."""
 import pytest
 
 pytestmark = pytest.mark.gpu
@@ -54,3 +56,41 @@ def test_release_other_stream_keeps_mine(cuda):
     vk.release_workspaces(all_streams=True)
     free2, _ = torch.cuda.mem_get_info()
     assert free2 - free_after_s2 >= 16 << 20
+
+
+def _timed_call(path, n=2048):
+    """(whole-call ms, bracketed-kernel ms) of one SGEMM n^3 on `path`."""
+    import torch
+    s = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(9)
+    A = torch.randn(n, n, device="cuda", generator=g)
+    B = torch.randn(n, n, device="cuda", generator=g)
+    C = torch.empty(n, n, device="cuda")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    for e in ev:
+        e.record(s)                        # creates the CUDA events
+    vk.set_path(path)
+    try:
+        vk.gemm_tensors(0, 0, n, n, n, 1.0, A, n, B, n, 0.0, C, n, stream=s)   # warm-up
+        torch.cuda.synchronize()
+        vk.set_kernel_events(ev[1], ev[2])
+        ev[0].record(s)
+        vk.gemm_tensors(0, 0, n, n, n, 1.0, A, n, B, n, 0.0, C, n, stream=s)
+        ev[3].record(s)
+        vk.set_kernel_events(None, None)
+        torch.cuda.synchronize()
+    finally:
+        vk.set_kernel_events(None, None)
+        vk.set_path(vk.PATH_AUTO)
+    assert vk.last_path() == path
+    return ev[0].elapsed_time(ev[3]), ev[1].elapsed_time(ev[2])
+
+
+def test_kernel_events_bracket_the_main_kernel(cuda):
+    # 3xTF32: split pre-pass, then the GEMM -- the hook brackets the GEMM only
+    call_ms, kern_ms = _timed_call(vk.PATH_TC)
+    assert 0.0 < kern_ms < call_ms
+    # exact SIMT: one kernel, so the bracket is nearly the whole call
+    call_ms, kern_ms = _timed_call(vk.PATH_SIMT)
+    assert 0.0 < kern_ms <= call_ms
+    assert kern_ms > 0.9 * call_ms

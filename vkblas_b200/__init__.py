@@ -76,6 +76,7 @@ def _load() -> C.CDLL:
     lib.vkblas_b200_device_status.argtypes = [i32]
     lib.vkblas_b200_device_status.restype = i32
     lib.vkblas_b200_launch_count.restype = C.c_uint64
+    lib.vkblas_b200_set_kernel_events.argtypes = [vp, vp]
     lib.vkblas_b200_release_workspaces.argtypes = [vp, i32]
     lib.vkblas_b200_release_workspaces.restype = i32
     lib.vkblas_b200_version.restype = C.c_char_p
@@ -138,6 +139,20 @@ def set_splitk(s: int) -> None:
 
 def device_status(clear: bool = True) -> int:
     return _get().vkblas_b200_device_status(1 if clear else 0)
+
+
+def set_kernel_events(start=None, end=None) -> None:
+    """Record torch.cuda.Event `start`/`end` around the main kernel of each
+    following call on this thread (None, None: off).  The events must have
+    been recorded once already, so that their CUDA handles exist."""
+    def handle(e):
+        if e is None:
+            return None
+        h = e.cuda_event
+        if not h:
+            raise VkblasError("record the event once before passing it")
+        return h
+    _get().vkblas_b200_set_kernel_events(handle(start), handle(end))
 
 
 def release_workspaces(stream=None, all_streams: bool = False) -> None:

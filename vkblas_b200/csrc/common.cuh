@@ -92,8 +92,12 @@ bool umma_uses_pair(const GemmProblem& p, int num_sms, bool split_ws);
 // cudaErrorNotSupported: the operands cannot be described to TMA (nothing launched).
 // test_stall: test hook, the producer leaves the first stage empty so the
 // MMA warp's bounded wait runs out (status DS_TIMEOUT_MMA) after 20 ms.
+// ev_start / ev_end (may be null): recorded on `s` right before the GEMM
+// kernel (after any 3xTF32 pre-pass) and right after it (after the split
+// reduce, if any) -- the measurement hook vkblas_b200_set_kernel_events.
 cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* workspace,
-                             void* split_workspace, bool test_stall, cudaStream_t s);
+                             void* split_workspace, bool test_stall, cudaStream_t s,
+                             cudaEvent_t ev_start = nullptr, cudaEvent_t ev_end = nullptr);
 // 2-D TMA tensor map over a 2-byte matrix [outer][inner] (row stride ld
 // elements), box [box_outer][box_inner], no swizzle.  False if the driver
 // entry point is missing or the layout cannot be described.

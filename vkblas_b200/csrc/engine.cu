@@ -140,6 +140,10 @@ struct ThreadState {
     int last_split = 1;
     int last_pair = 0;
     int test_stall = 0;
+    // Measurement hook (vkblas_b200_set_kernel_events): recorded around the
+    // main kernel of each call.
+    void* ev_start = nullptr;
+    void* ev_end = nullptr;
 };
 thread_local ThreadState tls;
 
@@ -189,6 +193,11 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
 
     cudaError_t e = cudaSuccess;
     int splitk = 0, split_used = 1, pair_used = 0;
+    const cudaEvent_t ev0 = reinterpret_cast<cudaEvent_t>(tls.ev_start);
+    const cudaEvent_t ev1 = reinterpret_cast<cudaEvent_t>(tls.ev_end);
+    auto rec = [&](cudaEvent_t ev) {
+        if (ev) cudaEventRecord(ev, s);
+    };
     if (path == VKBLAS_PATH_GEMV && p.dtype == DT_F32) {
         splitk = tls.splitk > 0 ? tls.splitk : cfg.gemv_splitk > 0 ? cfg.gemv_splitk
                                                                    : gemv_f32_auto_splitk(p, ds->num_sms);
@@ -199,7 +208,9 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
             ws = workspace(ds, 0, s, need);
             if (!ws) splitk = 1;
         }
+        rec(ev0);
         e = launch_gemv_f32(p, splitk, ws, s);
+        rec(ev1);
         split_used = splitk;
     } else if (path == VKBLAS_PATH_GEMV) {
         splitk = tls.splitk > 0 ? tls.splitk : cfg.gemv_splitk > 0 ? cfg.gemv_splitk
@@ -211,6 +222,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
             ws = workspace(ds, 0, s, need);
             if (!ws) splitk = 1;
         }
+        rec(ev0);
         e = launch_gemv(p, splitk, ws, ds->d_status, s);
         split_used = splitk;
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
@@ -222,6 +234,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
             cudaGetLastError();
             return VKBLAS_ERR_FALLBACK;
         }
+        rec(ev1);
     } else if (path == VKBLAS_PATH_TC) {
         const size_t need = umma_workspace_bytes(p);
         void* ws = need ? workspace(ds, 1, s, need) : nullptr;
@@ -229,7 +242,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
         void* wsplit = need_split ? workspace(ds, 2, s, need_split) : nullptr;   // null: no split
         e = (need && !ws) ? cudaErrorNotSupported
                           : launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, wsplit,
-                                             tls.test_stall != 0, s);
+                                             tls.test_stall != 0, s, ev0, ev1);
         split_used = wsplit ? umma_split_count(p, ds->num_sms) : 1;
         pair_used = umma_uses_pair(p, ds->num_sms, wsplit != nullptr) ? 1 : 0;
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
@@ -237,13 +250,17 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
             path = VKBLAS_PATH_SIMT;       // operands TMA cannot describe: exact SIMT path
             split_used = 1;
             pair_used = 0;
+            rec(ev0);
             e = launch_simt_gemm(p, s);
+            rec(ev1);
         } else if (e == cudaErrorNotSupported) {
             cudaGetLastError();
             return VKBLAS_ERR_FALLBACK;
         }
     } else {
+        rec(ev0);
         e = launch_simt_gemm(p, s);
+        rec(ev1);
     }
     if (cfg.trace)
         fprintf(stderr, "[vkblas] gemm %s %c%c M=%u N=%u K=%u lda=%u ldb=%u ldc=%u batch=%u path=%s%s%d -> %s\n",
@@ -479,6 +496,11 @@ VKB_EXPORT void vkblas_b200_set_splitk(int splitk) {
 }
 
 VKB_EXPORT void vkblas_b200_set_test_stall(int on) { tls.test_stall = on ? 1 : 0; }
+
+VKB_EXPORT void vkblas_b200_set_kernel_events(void* start, void* end) {
+    tls.ev_start = start;
+    tls.ev_end = end;
+}
 
 VKB_EXPORT int vkblas_b200_device_status(int clear) {
     int dev = 0;

@@ -1067,7 +1067,8 @@ size_t umma_workspace_bytes(const GemmProblem& p) {
 }
 
 cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status, void* ws,
-                             void* split_ws, bool test_stall, cudaStream_t s) {
+                             void* split_ws, bool test_stall, cudaStream_t s, cudaEvent_t ev_start,
+                             cudaEvent_t ev_end) {
     UmmaParams prm;
     memset(&prm, 0, sizeof(prm));
     prm.wait_limit_ns = test_stall ? TEST_WAIT_LIMIT_NS : WAIT_LIMIT_NS;
@@ -1182,6 +1183,7 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     const bool amn = a.mn_major, bmn = b.mn_major;
     cudaError_t e;
     const bool sm = ks.c_trans;
+    if (ev_start) cudaEventRecord(ev_start, s);        // after the 3xTF32 pre-pass
     switch (p.dtype) {
         case DT_F16:
             e = sm     ? launch_majors<K_F16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s)
@@ -1199,20 +1201,25 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
             break;
         default: return cudaErrorInvalidValue;
     }
-    if (e != cudaSuccess || prm.split_s <= 1) return e;
-    switch (p.dtype) {
-        case DT_F16:
-            return sm     ? launch_reduce<__half, BN_SM>(prm, s)
-                   : pair ? launch_reduce<__half, BN_16, 2 * BM>(prm, s)
-                          : launch_reduce<__half, BN_16>(prm, s);
-        case DT_BF16:
-            return sm     ? launch_reduce<__nv_bfloat16, BN_SM>(prm, s)
-                   : pair ? launch_reduce<__nv_bfloat16, BN_16, 2 * BM>(prm, s)
-                          : launch_reduce<__nv_bfloat16, BN_16>(prm, s);
-        default:
-            return pair ? launch_reduce<float, BN_TF32, 2 * BM>(prm, s)
-                        : launch_reduce<float, BN_TF32>(prm, s);
+    if (e == cudaSuccess && prm.split_s > 1) {
+        switch (p.dtype) {
+            case DT_F16:
+                e = sm     ? launch_reduce<__half, BN_SM>(prm, s)
+                    : pair ? launch_reduce<__half, BN_16, 2 * BM>(prm, s)
+                           : launch_reduce<__half, BN_16>(prm, s);
+                break;
+            case DT_BF16:
+                e = sm     ? launch_reduce<__nv_bfloat16, BN_SM>(prm, s)
+                    : pair ? launch_reduce<__nv_bfloat16, BN_16, 2 * BM>(prm, s)
+                           : launch_reduce<__nv_bfloat16, BN_16>(prm, s);
+                break;
+            default:
+                e = pair ? launch_reduce<float, BN_TF32, 2 * BM>(prm, s)
+                         : launch_reduce<float, BN_TF32>(prm, s);
+        }
     }
+    if (ev_end && e == cudaSuccess) cudaEventRecord(ev_end, s);
+    return e;
 }
 
 }  // namespace vkb
