@@ -256,6 +256,35 @@ def test_gemv_auto_split(shape, cuda):
     assert orc.rel_frobenius(got, want) <= 2e-3
 
 
+def test_decode_routing_large_n(cuda):
+    """9-16 tokens over >= 6 row-block CTAs per SM: the automatic path is the
+    small-M tcgen05 GEMM; an explicit GEMV split-K keeps the GEMV."""
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    M, N, K = 16, 6 * sms * 16, 1024
+    rng = np.random.default_rng(77)
+    X = orc.narrow(0, rng.uniform(-1, 1, M * K).astype(np.float32))
+    W = orc.narrow(0, (rng.uniform(-1, 1, N * K) * 0.05).astype(np.float32))
+    want = orc.hgemm_rowmajor_f64(0, 0, 1, M, N, K, 1.0, X, K, W, K, 0.0,
+                                  np.zeros(M * N, np.uint16), N)[0]
+    dX, dW = dev_u16(X, 0), dev_u16(W, 0)
+    vk.set_stream(torch.cuda.current_stream())
+    for splitk, path in ((0, vk.PATH_TC), (2, vk.PATH_GEMV)):
+        dC = dev_u16(np.zeros(M * N, np.uint16), 0)
+        vk.set_splitk(splitk)
+        try:
+            st = vk.gemm(vk.DT_F16, 0, 1, M, N, K, 1.0, dX.data_ptr(), K, dW.data_ptr(), K, 0.0,
+                         dC.data_ptr(), N)
+            torch.cuda.synchronize()
+        finally:
+            vk.set_splitk(0)
+        assert st == vk.VKBLAS_OK
+        assert vk.last_path() == path
+        check_status()
+        got = orc.widen(0, host_u16(dC)).reshape(M, N)
+        assert orc.rel_frobenius(got, want) <= 2e-3
+
+
 def test_config5_strided_batched_hgemm(cuda):
     """256 x 2048^3 fp16 NN strided-batched, sampled check."""
     import torch
