@@ -195,16 +195,53 @@ def dtype_of(t) -> int:
     return {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}[t.dtype]
 
 
+def _extent(rows: int, cols: int, ld: int, batch: int, stride: int) -> int:
+    """Elements a row-major operand addresses: the last batch entry's last row
+    ends at (batch - 1) * stride + (rows - 1) * ld + cols."""
+    return (batch - 1) * stride + (rows - 1) * ld + cols
+
+
+def _check_tensors(op_a, op_b, M, N, K, A, lda, B, ldb, Cout, ldc, batch, sa, sb, sc) -> None:
+    """Host-side checks of gemm_tensors' operands, before anything is launched:
+    CUDA tensors of one dtype on one device, contiguous (the engine addresses
+    their flat storage), and large enough for the addressed extents."""
+    ts = {"A": A, "B": B, "C": Cout}
+    for name, t in ts.items():
+        if not getattr(t, "is_cuda", False):
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous (flat storage, element strides)")
+    if not (A.dtype == B.dtype == Cout.dtype):
+        raise ValueError(f"dtypes differ: {A.dtype}, {B.dtype}, {Cout.dtype}")
+    if not (A.device == B.device == Cout.device):
+        raise ValueError(f"devices differ: {A.device}, {B.device}, {Cout.device}")
+    if min(M, N, K, batch) <= 0:
+        raise ValueError("M, N, K and batch must be positive")
+    ra, ca = (K, M) if op_a else (M, K)
+    rb, cb = (N, K) if op_b else (K, N)
+    for name, t, r, c, ld, st in (("A", A, ra, ca, lda, sa), ("B", B, rb, cb, ldb, sb),
+                                  ("C", Cout, M, N, ldc, sc)):
+        if ld < c:
+            raise ValueError(f"ld{name.lower()} = {ld} < {c}")
+        need = _extent(r, c, ld, batch, st)
+        if t.numel() < need:
+            raise ValueError(f"{name} holds {t.numel()} elements, the call addresses {need}")
+
+
 def gemm_tensors(op_a: int, op_b: int, M: int, N: int, K: int, alpha: float, A, lda: int, B,
                  ldb: int, beta: float, Cout, ldc: int, batch: int = 1, sa: int = 0, sb: int = 0,
                  sc: int = 0, stream=None) -> None:
     """Engine call on torch CUDA tensors (flat storage, element strides), on
-    ``stream`` (default: torch's current stream).  Raises on a non-OK status."""
+    ``stream`` (default: torch's current stream), on the tensors' device.
+    Raises ValueError for operands that do not fit the call, VkblasError on a
+    non-OK status."""
     import torch
-    if stream is None:
-        stream = torch.cuda.current_stream()
-    set_stream(stream)
-    st = gemm(dtype_of(A), op_a, op_b, M, N, K, alpha, A.data_ptr(), lda, B.data_ptr(), ldb, beta,
-              Cout.data_ptr(), ldc, batch, sa, sb, sc)
+    _check_tensors(op_a, op_b, M, N, K, A, lda, B, ldb, Cout, ldc, batch, sa, sb, sc)
+    with torch.cuda.device(A.device):
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        set_stream(stream)
+        st = gemm(dtype_of(A), op_a, op_b, M, N, K, alpha, A.data_ptr(), lda, B.data_ptr(), ldb,
+                  beta, Cout.data_ptr(), ldc, batch, sa, sb, sc)
     if st != VKBLAS_OK:
         raise VkblasError(f"vkblas gemm returned status {st}")
