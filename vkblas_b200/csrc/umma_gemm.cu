@@ -34,6 +34,8 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -857,6 +859,9 @@ cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cuda
                 return cudaErrorNotSupported;
             }
             max_clusters[dev & 63] = n;
+            if (getenv("VKBLAS_TRACE"))
+                fprintf(stderr, "[vkblas] device %d: %d resident 2-CTA clusters for %s (%d SMs)\n",
+                        dev, n, KIND == K_TF32X3 ? "3xTF32" : "kind::f16", num_sms);
         }
         attr_done.fetch_or(bit);
     }
