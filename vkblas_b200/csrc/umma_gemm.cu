@@ -30,7 +30,8 @@
 // main loop accumulates A_small*B_big + A_big*B_small + A_big*B_big into one
 // fp32 TMEM accumulator.
 //
-// No cluster multicast anywhere: each CTA issues its own TMA loads.
+// No TMA load uses cluster multicast: each CTA issues its own loads.  The only
+// multicast is tcgen05.commit's, which signals both CTAs of a pair.
 #include <cudaTypedefs.h>
 
 #include <atomic>
