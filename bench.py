@@ -306,6 +306,8 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-seconds", type=float, default=60.0,
+                    help="--impl reference: host CPU time to spend over all timed steps")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -320,7 +322,7 @@ def main() -> int:
         for _ in range(args.warmup):
             ref.sample(0.2)
         info = None
-        per_step = max(0.2, 60.0 / max(1, args.steps))
+        per_step = max(0.2, args.ref_seconds / max(1, args.steps))
         for _ in range(args.steps):
             tf, info = ref.sample(per_step)
             tfs.append(tf)
