@@ -368,6 +368,7 @@ def main() -> int:
         step(i)
     torch.cuda.synchronize()
     path = vk.PATH_NAMES[vk.last_path()]
+    tile_n, pair, split = vk.last_tile_n(), vk.last_pair(), vk.last_split()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -463,14 +464,19 @@ def main() -> int:
     gemm_tflops = FLOP_PER_GEMM / (gemm_ms / 1e3) / 1e12
     traffic, traffic_src = None, None
     if path == "tc":
-        kernel_name = "3xTF32 tcgen05 SGEMM (umma_gemm_kernel, CTA pairs)"
+        tiles = f"{256 if pair else 128}x{tile_n} tiles" + (" on CTA pairs" if pair else "")
+        kernel_name = f"3xTF32 tcgen05 SGEMM (umma_gemm_kernel, {tiles}" + (
+            f"; last wave split {split} ways, then split_reduce_kernel)" if split > 1 else ")")
         peak = peaks["bf16_tflops"] / 2.0 / 3.0
         peak_note = (f"{peaks_kind} bf16 burst {peaks['bf16_tflops']} TF / 2 (TF32 rate) / 3 "
                      "(three TF32 MMAs per useful FLOP)")
-        # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel
-        # at this shape (859.3 MB + 64.1 MB), from the committed ncu capture
-        traffic = 923.4e6
-        traffic_src = "ncu --set full, profiles/umma_gemm_tf32x3_sgemm_nn_4096.md"
+        if pair and tile_n == 128:
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel
+            # at this shape (859.3 MB + 64.1 MB), from the committed ncu capture
+            traffic = 923.4e6
+            traffic_src = "ncu --set full, profiles/umma_gemm_tf32x3_sgemm_nn_4096.md"
+        else:
+            traffic_src = "no ncu capture of this tile configuration"
     else:
         kernel_name = "FFMA SIMT SGEMM"
         peak = 148 * 128 * 2 * (peaks.get("sm_max_mhz", 1965.0) * 1e6) / 1e12

@@ -86,6 +86,11 @@ int vkblas_b200_last_split(void);
 /* 1 when that call ran on 2-CTA clusters (tcgen05 cta_group::2, 256-row
  * tiles: each CTA loads half of the B tile), else 0. */
 int vkblas_b200_last_pair(void);
+/* N width of that call's tensor-core tile: 256 for fp16/bf16 and for 3xTF32
+ * on CTA pairs with N >= 256, 128 for other 3xTF32 tiles, 64 for small-M
+ * transposed tiles (over the swapped problem); 0 when the call did not run on
+ * the tensor-core path. */
+int vkblas_b200_last_tile_n(void);
 /* Thread-local split-K factor for the GEMV path: 0 = automatic, else 1..16. */
 void vkblas_b200_set_splitk(int splitk);
 

@@ -237,3 +237,33 @@ def test_tc_pair_wave_tail_split(dtype, cuda):
     """75 pair tiles (one per batch entry) on 74 SM pairs: whole waves run
     unsplit, only the last pair tile is split along K."""
     _run(dtype, 0, 0, 256, 40, 4096, 1.0, 0.0, batch=75, split=True, pair=True)
+
+
+def test_tf32_transposed_split_beyond_grid_y_limit(cuda):
+    """K above 65535 * 64 with both fp32 operands MN-major (op_a = T, op_b = N,
+    the shape of a weight gradient over millions of tokens): the transposing
+    3xTF32 pre-pass strides over k tiles instead of needing a larger grid, so
+    the tail beyond the first 65535 tiles reaches the planes.  Checked against
+    a double-precision product (numpy; the C oracle is far slower at this K)."""
+    import torch
+    M = N = 32
+    K = 65537 * 64
+    rng = np.random.default_rng(17)
+    A = rng.standard_normal(K * M, dtype=np.float32)      # A[k * M + m]
+    B = rng.standard_normal(K * N, dtype=np.float32)      # B[k * N + n]
+    dA, dB = dev(A), dev(B)
+    dC = torch.zeros(M * N, dtype=torch.float32, device="cuda")
+    vk.set_path(vk.PATH_TC)
+    try:
+        vk.set_stream(torch.cuda.current_stream())
+        st = vk.gemm(vk.DT_F32, 1, 0, M, N, K, 1.0, dA.data_ptr(), M, dB.data_ptr(), N, 0.0,
+                     dC.data_ptr(), N, 1, 0, 0, 0)
+        torch.cuda.synchronize()
+    finally:
+        vk.set_path(vk.PATH_AUTO)
+    assert st == vk.VKBLAS_OK, f"status {st}"
+    assert vk.last_path() == vk.PATH_TC
+    check_status()
+    want = A.reshape(K, M).astype(np.float64).T @ B.reshape(K, N).astype(np.float64)
+    err = orc.rel_frobenius(host(dC).reshape(M, N), want)
+    assert err <= TOL[vk.DT_F32], f"relative error {err}"

@@ -71,6 +71,7 @@ def _load() -> C.CDLL:
     lib.vkblas_b200_last_path.restype = i32
     lib.vkblas_b200_last_split.restype = i32
     lib.vkblas_b200_last_pair.restype = i32
+    lib.vkblas_b200_last_tile_n.restype = i32
     lib.vkblas_b200_set_splitk.argtypes = [i32]
     lib.vkblas_b200_set_test_stall.argtypes = [i32]
     lib.vkblas_b200_device_status.argtypes = [i32]
@@ -131,6 +132,11 @@ def last_split() -> int:
 def last_pair() -> bool:
     """Whether this thread's last call ran on 2-CTA clusters (256-row tiles)."""
     return bool(_get().vkblas_b200_last_pair())
+
+
+def last_tile_n() -> int:
+    """N width of the tensor-core tile of this thread's last call (0: not tensor-core)."""
+    return _get().vkblas_b200_last_tile_n()
 
 
 def set_splitk(s: int) -> None:

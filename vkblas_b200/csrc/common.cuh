@@ -89,6 +89,7 @@ size_t umma_split_workspace_bytes(const GemmProblem& p, int num_sms);
 int umma_split_count(const GemmProblem& p, int num_sms);   // K splits of the last wave (1 = none)
 // True when the call runs on 2-CTA clusters (256-row tiles, cta_group::2).
 bool umma_uses_pair(const GemmProblem& p, int num_sms, bool split_ws);
+int umma_tile_n(const GemmProblem& p);                      // N width of the kernel's tile
 // cudaErrorNotSupported: the operands cannot be described to TMA (nothing launched).
 // test_stall: test hook, the producer leaves the first stage empty so the
 // MMA warp's bounded wait runs out (status DS_TIMEOUT_MMA) after 20 ms.

@@ -19,6 +19,7 @@
 // VKBLAS_HGEMM=simt|tc|auto, VKBLAS_GEMV=0|1, VKBLAS_GEMV_SPLITK=n,
 // VKBLAS_TC_SPLIT=0|1 (K-split of the tensor-core GEMM's last wave),
 // VKBLAS_TC_PAIR=0|1 (256-row tiles on 2-CTA clusters; read in umma_gemm.cu),
+// VKBLAS_TF32_WIDE=0|1 (256 x 256 3xTF32 pair tiles; read in umma_gemm.cu),
 // VKBLAS_TRACE=1 (one line per call on stderr).
 #include <atomic>
 #include <cstdio>
@@ -139,6 +140,7 @@ struct ThreadState {
     int last = VKBLAS_PATH_AUTO;
     int last_split = 1;
     int last_pair = 0;
+    int last_tile_n = 0;
     int test_stall = 0;
     // Measurement hook (vkblas_b200_set_kernel_events): recorded around the
     // main kernel of each call.
@@ -201,7 +203,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     if (!path) return VKBLAS_ERR_FALLBACK;
 
     cudaError_t e = cudaSuccess;
-    int splitk = 0, split_used = 1, pair_used = 0;
+    int splitk = 0, split_used = 1, pair_used = 0, tile_n = 0;
     const cudaEvent_t ev0 = reinterpret_cast<cudaEvent_t>(tls.ev_start);
     const cudaEvent_t ev1 = reinterpret_cast<cudaEvent_t>(tls.ev_end);
     auto rec = [&](cudaEvent_t ev) {
@@ -254,11 +256,13 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
                                              tls.test_stall != 0, s, ev0, ev1);
         split_used = wsplit ? umma_split_count(p, ds->num_sms) : 1;
         pair_used = umma_uses_pair(p, ds->num_sms, wsplit != nullptr) ? 1 : 0;
+        tile_n = umma_tile_n(p);
         if (e == cudaErrorNotSupported && forced == VKBLAS_PATH_AUTO) {
             cudaGetLastError();
             path = VKBLAS_PATH_SIMT;       // operands TMA cannot describe: exact SIMT path
             split_used = 1;
             pair_used = 0;
+            tile_n = 0;
             rec(ev0);
             e = launch_simt_gemm(p, s);
             rec(ev1);
@@ -284,6 +288,7 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
     tls.last = path;
     tls.last_split = split_used;
     tls.last_pair = pair_used;
+    tls.last_tile_n = tile_n;
     return VKBLAS_OK;
 }
 
@@ -500,6 +505,7 @@ VKB_EXPORT int vkblas_b200_get_path(void) { return tls.path; }
 VKB_EXPORT int vkblas_b200_last_path(void) { return tls.last; }
 VKB_EXPORT int vkblas_b200_last_split(void) { return tls.last_split; }
 VKB_EXPORT int vkblas_b200_last_pair(void) { return tls.last_pair; }
+VKB_EXPORT int vkblas_b200_last_tile_n(void) { return tls.last_tile_n; }
 VKB_EXPORT void vkblas_b200_set_splitk(int splitk) {
     tls.splitk = splitk < 0 ? 0 : splitk > 16 ? 16 : splitk;
 }

@@ -209,13 +209,23 @@ struct Cfg {
     // segments in fp32 with round-to-nearest; 2-byte kinds keep one
     // accumulator per tile (their tolerance is far above that error).
     static constexpr uint32_t SEG_KB = (KIND == K_TF32X3) ? 8u : 0u;
-    static constexpr uint32_t NBUF = SEG_KB ? 4u : 2u;            // TMEM accumulator buffers
+    // TMEM accumulator buffers: 512 columns hold four 128-wide or two 256-wide.
+    static constexpr uint32_t NBUF = (SEG_KB && BN <= 128) ? 4u : 2u;
     // Epilogue warps: 4 (one per TMEM lane quarter), or 8 for the segmented
     // epilogue, where two warps share a quarter and each keeps the fp32 sums of
     // half of the tile's columns in registers.
     static constexpr int EPI_WARPS = SEG_KB ? 8 : 4;
     static constexpr int EPI_COLS = BN * 4 / EPI_WARPS;          // columns per epilogue thread
-    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    // A 256-wide segmented tile keeps 128 fp32 sums per epilogue thread, more
+    // than an even share of the register file allows.  Its block has 12 warps:
+    // warpgroup 0 (TMA producer, MMA issuer, two idle warps) drops to REGS_LOW
+    // registers a thread and the two epilogue warpgroups rise to REGS_HIGH
+    // (setmaxnreg).  The host launches it only when the split fits the
+    // registers the block is launched with (launch_kind).
+    static constexpr bool REG_SPLIT = SEG_KB != 0 && EPI_COLS > 64;
+    static constexpr int EPI_WARP0 = REG_SPLIT ? 4 : 2;           // first epilogue warp
+    static constexpr int THREADS = 32 * EPI_WARP0 + 32 * EPI_WARPS;
+    static constexpr uint32_t REGS_LOW = 56, REGS_HIGH = 208;
     static constexpr uint32_t TMEM_COLS = NBUF * BN;                // 512
     static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
     static constexpr uint32_t IDESC =
@@ -225,7 +235,10 @@ struct Cfg {
     static constexpr uint32_t TEMPTY_COUNT = (PAIR ? 2u : 1u) * 32u * EPI_WARPS;
     static constexpr uint32_t SLAB = BK * ROW_BYTES;  // MN-major: one 128-byte-wide slab
     static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
-    static_assert(SEG_KB == 0 || EPI_COLS <= 64, "segmented epilogue keeps EPI_COLS fp32 sums per thread");
+    static_assert(SEG_KB == 0 || EPI_COLS <= 128, "segmented epilogue keeps EPI_COLS fp32 sums per thread");
+    static_assert(!REG_SPLIT || (REGS_LOW % 8 == 0 && REGS_HIGH % 8 == 0 && REGS_LOW >= 24 &&
+                                 REGS_HIGH <= 256 && THREADS == 384),
+                  "register split: one 128-thread warpgroup low, two high");
 };
 
 template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
@@ -299,171 +312,181 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
     // Let a programmatically dependent split_reduce_kernel get resident; it
     // waits (griddepcontrol.wait) until this grid has finished and flushed.
     if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-
-    if (warp == 0) {
-        // ------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            uint32_t stage = 0, phase = 0;
-            uint32_t issued_mask = 0, issued_parity = 0;   // per stage: issued ever / last parity
-            bool ok = true;
-            for (uint32_t u = unit0; ok && u < p.total_units; u += ustride) {
-                uint32_t t, sp, ukb0, ukb1, b, mb, nb;
-                unit_info(p, u, t, sp, ukb0, ukb1);
-                tile_coords(p, t, b, mb, nb);
-                const int32_t m0 = (int32_t)(mb * C_::BM_TILE + rank * BM);
-                const int32_t n0 = (int32_t)(nb * BN + rank * C_::BNC);
-                const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
-                const uint32_t len = ukb1 - ukb0;
-                // Only the weight-streaming small-M tiles (BN = 64) rotate: all
-                // tiles start together, and in plain order every weight row
-                // would be read at the same k offset at the same time, which
-                // loads the HBM channels unevenly.
-                const uint32_t rot = (BN == 64 && p.k_rot_mul) ? (t * p.k_rot_mul) % len : 0u;
-                for (uint32_t i = 0; i < len; i++) {
-                    const uint32_t kb = ukb0 + (i + rot < len ? i + rot : i + rot - len);
-                    if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
-                                  DS_TIMEOUT_PRODUCER, p.wait_limit_ns)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t fb = to_issuer(full_bar(stage));
-                    if (p.test_skip_first_load && u == unit0 && i == 0) {
-                        // Test hook: leave this stage empty so its consumer's
-                        // bounded wait runs out (no copy is issued).
+    // Warp roles.  With a register split, setmaxnreg opens each warpgroup's
+    // branch, so that the compiler allocates each branch within its limit.
+    if (warp < C_::EPI_WARP0) {
+        if constexpr (C_::REG_SPLIT)
+            asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C_::REGS_LOW));
+        if (warp == 0) {
+            // ------------------------------------------------------ TMA producer
+            if (lane == 0) {
+                uint32_t stage = 0, phase = 0;
+                uint32_t issued_mask = 0, issued_parity = 0;   // per stage: issued ever / last parity
+                bool ok = true;
+                for (uint32_t u = unit0; ok && u < p.total_units; u += ustride) {
+                    uint32_t t, sp, ukb0, ukb1, b, mb, nb;
+                    unit_info(p, u, t, sp, ukb0, ukb1);
+                    tile_coords(p, t, b, mb, nb);
+                    const int32_t m0 = (int32_t)(mb * C_::BM_TILE + rank * BM);
+                    const int32_t n0 = (int32_t)(nb * BN + rank * C_::BNC);
+                    const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
+                    const uint32_t len = ukb1 - ukb0;
+                    // Only the weight-streaming small-M tiles (BN = 64) rotate: all
+                    // tiles start together, and in plain order every weight row
+                    // would be read at the same k offset at the same time, which
+                    // loads the HBM channels unevenly.
+                    const uint32_t rot = (BN == 64 && p.k_rot_mul) ? (t * p.k_rot_mul) % len : 0u;
+                    for (uint32_t i = 0; i < len; i++) {
+                        const uint32_t kb = ukb0 + (i + rot < len ? i + rot : i + rot - len);
+                        if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
+                                      DS_TIMEOUT_PRODUCER, p.wait_limit_ns)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t fb = to_issuer(full_bar(stage));
+                        if (p.test_skip_first_load && u == unit0 && i == 0) {
+                            // Test hook: leave this stage empty so its consumer's
+                            // bounded wait runs out (no copy is issued).
+                            if (++stage == STAGES) {
+                                stage = 0;
+                                phase ^= 1u;
+                            }
+                            continue;
+                        }
+                        // The issuer expects both CTAs' bytes of a pair stage.
+                        if (issuer) mbar_arrive_expect_tx(full_bar(stage), (PAIR ? 2u : 1u) * C_::STAGE_BYTES);
+                        const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
+                        const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
+                        const int32_t k0 = (int32_t)(kb * C_::BK);
+                        auto load = [&](uint32_t dst, const CUtensorMap* m, int32_t c0, int32_t c1,
+                                        int32_t c2) {
+                            if constexpr (PAIR) tma_load_3d_pair(dst, m, fb, c0, c1, c2);
+                            else tma_load_3d(dst, m, fb, c0, c1, c2);
+                        };
+    #pragma unroll
+                        for (int pl = 0; pl < C_::PLANES; pl++) {
+                            if (!A_MN) {
+                                load(sA + pl * C_::A_PLANE, &p.tmA[pl], k0, m0, ba);
+                            } else {
+    #pragma unroll
+                                for (int j = 0; j < BM / C_::EPB; j++)
+                                    load(sA + pl * C_::A_PLANE + j * C_::SLAB, &p.tmA[pl],
+                                         m0 + j * C_::EPB, k0, ba);
+                            }
+                            if (!B_MN) {
+                                load(sB + pl * C_::B_PLANE, &p.tmB[pl], k0, n0, bb);
+                            } else {
+    #pragma unroll
+                                for (int j = 0; j < C_::BNC / C_::EPB; j++)
+                                    load(sB + pl * C_::B_PLANE + j * C_::SLAB, &p.tmB[pl],
+                                         n0 + j * C_::EPB, k0, bb);
+                            }
+                        }
+                        issued_mask |= 1u << stage;
+                        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                         if (++stage == STAGES) {
                             stage = 0;
                             phase ^= 1u;
                         }
-                        continue;
-                    }
-                    // The issuer expects both CTAs' bytes of a pair stage.
-                    if (issuer) mbar_arrive_expect_tx(full_bar(stage), (PAIR ? 2u : 1u) * C_::STAGE_BYTES);
-                    const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
-                    const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
-                    const int32_t k0 = (int32_t)(kb * C_::BK);
-                    auto load = [&](uint32_t dst, const CUtensorMap* m, int32_t c0, int32_t c1,
-                                    int32_t c2) {
-                        if constexpr (PAIR) tma_load_3d_pair(dst, m, fb, c0, c1, c2);
-                        else tma_load_3d(dst, m, fb, c0, c1, c2);
-                    };
-#pragma unroll
-                    for (int pl = 0; pl < C_::PLANES; pl++) {
-                        if (!A_MN) {
-                            load(sA + pl * C_::A_PLANE, &p.tmA[pl], k0, m0, ba);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < BM / C_::EPB; j++)
-                                load(sA + pl * C_::A_PLANE + j * C_::SLAB, &p.tmA[pl],
-                                     m0 + j * C_::EPB, k0, ba);
-                        }
-                        if (!B_MN) {
-                            load(sB + pl * C_::B_PLANE, &p.tmB[pl], k0, n0, bb);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < C_::BNC / C_::EPB; j++)
-                                load(sB + pl * C_::B_PLANE + j * C_::SLAB, &p.tmB[pl],
-                                     n0 + j * C_::EPB, k0, bb);
-                        }
-                    }
-                    issued_mask |= 1u << stage;
-                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
                     }
                 }
+                // Never leave with copies in flight: wait for the last fill of every
+                // stage (the issuer's full barrier; in the other CTA of a pair, the
+                // stage's release by the issuer's MMAs, which follows its landing).
+                for (int s = 0; s < STAGES; s++)
+                    if (issued_mask & (1u << s))
+                        drain_bar_wait(issuer ? full_bar(s) : empty_bar(s), (issued_parity >> s) & 1u,
+                                       p.status, DS_TIMEOUT_PRODUCER, DRAIN_LIMIT_NS);
             }
-            // Never leave with copies in flight: wait for the last fill of every
-            // stage (the issuer's full barrier; in the other CTA of a pair, the
-            // stage's release by the issuer's MMAs, which follows its landing).
-            for (int s = 0; s < STAGES; s++)
-                if (issued_mask & (1u << s))
-                    drain_bar_wait(issuer ? full_bar(s) : empty_bar(s), (issued_parity >> s) & 1u,
-                                   p.status, DS_TIMEOUT_PRODUCER, DRAIN_LIMIT_NS);
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------- MMA issuer
-        if (lane == 0 && issuer) {
-            uint32_t stage = 0, phase = 0, u = 0;          // u: accumulator hand-overs so far
-            bool ok = true;
-            for (uint32_t w = unit0; ok && w < p.total_units; w += ustride) {
-                uint32_t t, sp, ukb0, ukb1;
-                unit_info(p, w, t, sp, ukb0, ukb1);
-                const uint32_t seg_kb = C_::SEG_KB ? C_::SEG_KB : (ukb1 - ukb0);
-                const uint32_t nseg = (ukb1 - ukb0 + seg_kb - 1) / seg_kb;
-                for (uint32_t sg = 0; ok && sg < nseg; sg++, u++) {
-                    const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
-                    if (!wait_bar(tempty_bar(buf), bph ^ 1u, abort_flag, p.status, DS_TIMEOUT_MMA,
-                                  p.wait_limit_ns)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t d = tmem_base + buf * BN;
-                    const uint32_t kb0 = ukb0 + sg * seg_kb;
-                    const uint32_t kb1 = min(ukb1, kb0 + seg_kb);
-                    for (uint32_t kb = kb0; kb < kb1; kb++) {
-                        if (!wait_bar(full_bar(stage), phase, abort_flag, p.status, DS_TIMEOUT_MMA,
+        } else if (warp == 1) {
+            // ------------------------------------------------------- MMA issuer
+            if (lane == 0 && issuer) {
+                uint32_t stage = 0, phase = 0, u = 0;          // u: accumulator hand-overs so far
+                bool ok = true;
+                for (uint32_t w = unit0; ok && w < p.total_units; w += ustride) {
+                    uint32_t t, sp, ukb0, ukb1;
+                    unit_info(p, w, t, sp, ukb0, ukb1);
+                    const uint32_t seg_kb = C_::SEG_KB ? C_::SEG_KB : (ukb1 - ukb0);
+                    const uint32_t nseg = (ukb1 - ukb0 + seg_kb - 1) / seg_kb;
+                    for (uint32_t sg = 0; ok && sg < nseg; sg++, u++) {
+                        const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
+                        if (!wait_bar(tempty_bar(buf), bph ^ 1u, abort_flag, p.status, DS_TIMEOUT_MMA,
                                       p.wait_limit_ns)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
-                        const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
-#pragma unroll
-                        for (int j = 0; j < C_::KSTEPS; j++) {
-                            uint64_t ad[C_::PLANES], bd[C_::PLANES];
-#pragma unroll
-                            for (int pl = 0; pl < C_::PLANES; pl++) {
-                                ad[pl] = A_MN ? smem_desc_sw128(sA + pl * C_::A_PLANE + j * C_::UK * ROW_BYTES,
-                                                                C_::SLAB, 1024)
-                                              : smem_desc_sw128(sA + pl * C_::A_PLANE + j * 32, 16, 1024);
-                                bd[pl] = B_MN ? smem_desc_sw128(sB + pl * C_::B_PLANE + j * C_::UK * ROW_BYTES,
-                                                                C_::SLAB, 1024)
-                                              : smem_desc_sw128(sB + pl * C_::B_PLANE + j * 32, 16, 1024);
+                        const uint32_t d = tmem_base + buf * BN;
+                        const uint32_t kb0 = ukb0 + sg * seg_kb;
+                        const uint32_t kb1 = min(ukb1, kb0 + seg_kb);
+                        for (uint32_t kb = kb0; kb < kb1; kb++) {
+                            if (!wait_bar(full_bar(stage), phase, abort_flag, p.status, DS_TIMEOUT_MMA,
+                                          p.wait_limit_ns)) {
+                                ok = false;
+                                break;
                             }
-                            const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
-                            if constexpr (KIND == K_TF32X3) {
-                                if constexpr (PAIR) {
-                                    mma_tf32_pair(d, ad[1], bd[0], C_::IDESC, first);
-                                    mma_tf32_pair(d, ad[0], bd[1], C_::IDESC, 1u);
-                                    mma_tf32_pair(d, ad[0], bd[0], C_::IDESC, 1u);
-                                } else {
-                                    mma_tf32(d, ad[1], bd[0], C_::IDESC, first);   // A_small * B_big
-                                    mma_tf32(d, ad[0], bd[1], C_::IDESC, 1u);      // A_big * B_small
-                                    mma_tf32(d, ad[0], bd[0], C_::IDESC, 1u);      // A_big * B_big
+                            tc_fence_after();
+                            const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
+                            const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
+    #pragma unroll
+                            for (int j = 0; j < C_::KSTEPS; j++) {
+                                uint64_t ad[C_::PLANES], bd[C_::PLANES];
+    #pragma unroll
+                                for (int pl = 0; pl < C_::PLANES; pl++) {
+                                    ad[pl] = A_MN ? smem_desc_sw128(sA + pl * C_::A_PLANE + j * C_::UK * ROW_BYTES,
+                                                                    C_::SLAB, 1024)
+                                                  : smem_desc_sw128(sA + pl * C_::A_PLANE + j * 32, 16, 1024);
+                                    bd[pl] = B_MN ? smem_desc_sw128(sB + pl * C_::B_PLANE + j * C_::UK * ROW_BYTES,
+                                                                    C_::SLAB, 1024)
+                                                  : smem_desc_sw128(sB + pl * C_::B_PLANE + j * 32, 16, 1024);
                                 }
-                            } else {
-                                if constexpr (PAIR) mma_f16_pair(d, ad[0], bd[0], C_::IDESC, first);
-                                else mma_f16(d, ad[0], bd[0], C_::IDESC, first);
+                                const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
+                                if constexpr (KIND == K_TF32X3) {
+                                    if constexpr (PAIR) {
+                                        mma_tf32_pair(d, ad[1], bd[0], C_::IDESC, first);
+                                        mma_tf32_pair(d, ad[0], bd[1], C_::IDESC, 1u);
+                                        mma_tf32_pair(d, ad[0], bd[0], C_::IDESC, 1u);
+                                    } else {
+                                        mma_tf32(d, ad[1], bd[0], C_::IDESC, first);   // A_small * B_big
+                                        mma_tf32(d, ad[0], bd[1], C_::IDESC, 1u);      // A_big * B_small
+                                        mma_tf32(d, ad[0], bd[0], C_::IDESC, 1u);      // A_big * B_big
+                                    }
+                                } else {
+                                    if constexpr (PAIR) mma_f16_pair(d, ad[0], bd[0], C_::IDESC, first);
+                                    else mma_f16(d, ad[0], bd[0], C_::IDESC, first);
+                                }
+                            }
+                            if constexpr (PAIR) tc_commit_pair_mc(empty_bar(stage), 0x3);   // both CTAs' stage
+                            else tc_commit(empty_bar(stage));
+                            if (++stage == STAGES) {
+                                stage = 0;
+                                phase ^= 1u;
                             }
                         }
-                        if constexpr (PAIR) tc_commit_pair_mc(empty_bar(stage), 0x3);   // both CTAs' stage
-                        else tc_commit(empty_bar(stage));
-                        if (++stage == STAGES) {
-                            stage = 0;
-                            phase ^= 1u;
-                        }
+                        if (!ok) break;
+                        if constexpr (PAIR) tc_commit_pair_mc(tfull_bar(buf), 0x3);    // both epilogues
+                        else tc_commit(tfull_bar(buf));
                     }
-                    if (!ok) break;
-                    if constexpr (PAIR) tc_commit_pair_mc(tfull_bar(buf), 0x3);    // both epilogues
-                    else tc_commit(tfull_bar(buf));
                 }
+                // Never leave with MMAs in flight.
+                if constexpr (PAIR) tc_commit_pair(drain_bar);
+                else tc_commit(drain_bar);
+                drain_bar_wait(drain_bar, 0, p.status, DS_TIMEOUT_MMA, DRAIN_LIMIT_NS);
             }
-            // Never leave with MMAs in flight.
-            if constexpr (PAIR) tc_commit_pair(drain_bar);
-            else tc_commit(drain_bar);
-            drain_bar_wait(drain_bar, 0, p.status, DS_TIMEOUT_MMA, DRAIN_LIMIT_NS);
         }
     } else {
+        if constexpr (C_::REG_SPLIT)
+            asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C_::REGS_HIGH));
         // --------------------------------------------------------- epilogue
         float alpha = p.alpha, beta = p.beta;
         load_scalars(p.d_alpha, p.d_beta, alpha, beta);
         const uint32_t q = (uint32_t)(warp & 3);          // TMEM lane quarter of this warp
-        const uint32_t col0 = (uint32_t)((warp - 2) / 4) * C_::EPI_COLS;   // this warp's columns
+        const uint32_t col0 = (uint32_t)((warp - C_::EPI_WARP0) / 4) * C_::EPI_COLS;   // this warp's columns
         const uint32_t row = q * 32u + (uint32_t)lane;
         const uint32_t lane_off = (q * 32u) << 16;
+        // Only 2-byte small-M GEMMs run transposed; fp32 kernels leave that
+        // store out, which keeps the segment sums in registers.
+        constexpr bool IS_F32 = KIND == K_TF32X3;
         TOut* Cbase = reinterpret_cast<TOut*>(p.C);
         uint32_t u = 0;                                       // accumulator hand-overs
         bool ok = true;
@@ -509,7 +532,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                     } else {
                         const uint32_t n0 = nb * BN + col0 + c * 32;
                         if (m < p.M && n0 < p.N) {
-                            if (p.c_trans)
+                            if (!IS_F32 && p.c_trans)
                                 store_col32<TOut>(cb, m, n0, p.ldc, v, min(32u, p.N - n0), alpha, beta);
                             else
                                 store_row32<TOut>(crow + n0, v, min(32u, p.N - n0), p.c_vec_ok != 0,
@@ -521,7 +544,14 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                 release(buf);
                 u++;
             } else {
+                // -0 is the exact identity of fp32 addition (-0 + x == x for
+                // every x, -0 included): the first segment's sums come through
+                // unchanged, and an unconditional add keeps them in registers.
                 float sum[C_::EPI_COLS / 32][32];
+#pragma unroll
+                for (int c = 0; c < C_::EPI_COLS / 32; c++)
+#pragma unroll
+                    for (int i = 0; i < 32; i++) sum[c][i] = -0.f;
                 const uint32_t nseg = (ukb1 - ukb0 + C_::SEG_KB - 1) / C_::SEG_KB;
                 for (uint32_t sg = 0; sg < nseg; sg++, u++) {
                     const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
@@ -537,8 +567,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; i++)
-                            sum[c][i] = sg ? __fadd_rn(sum[c][i], __uint_as_float(r[i]))
-                                           : __uint_as_float(r[i]);
+                            sum[c][i] = __fadd_rn(sum[c][i], __uint_as_float(r[i]));
                     }
                     tc_fence_before();
                     release(buf);
@@ -551,7 +580,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                     } else {
                         const uint32_t n0 = nb * BN + col0 + c * 32;
                         if (m < p.M && n0 < p.N) {
-                            if (p.c_trans)
+                            if (!IS_F32 && p.c_trans)
                                 store_col32<TOut>(cb, m, n0, p.ldc, sum[c], min(32u, p.N - n0),
                                                   alpha, beta);
                             else
@@ -699,7 +728,9 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, uint32_t rows, 
 // Same split for an MN-major operand (src[b][k][ld], MN contiguous), written
 // K-major (out[b][mn][ldo], K contiguous) so that the tf32 MMAs always read
 // K-major operands.  A 64x64 tile goes through shared memory; both the global
-// reads (along MN) and the writes (along K) are 128-bit when aligned.
+// reads (along MN) and the writes (along K) are 128-bit when aligned.  Blocks
+// stride over batch entries (z) and over 64-wide k tiles (y), so that K beyond
+// 65535 * 64 (a weight gradient over millions of tokens) needs no larger grid.
 constexpr int TT = 64;
 __global__ void __launch_bounds__(256) split_tf32_t_kernel(const float* __restrict__ src,
                                                            uint32_t K, uint32_t MN, uint32_t ld,
@@ -707,11 +738,12 @@ __global__ void __launch_bounds__(256) split_tf32_t_kernel(const float* __restri
                                                            uint32_t ldo, float* __restrict__ big,
                                                            float* __restrict__ small) {
     __shared__ float tile[TT][TT + 1];                // [k][mn]
-    const uint32_t mn0 = blockIdx.x * TT, k0 = blockIdx.y * TT;
+    const uint32_t mn0 = blockIdx.x * TT;
     const uint32_t tx = threadIdx.x & 15, ty = threadIdx.x >> 4;    // 16 x 16
     const bool vec_in = (ld & 3u) == 0 && (bstride & 3) == 0 &&
                         (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-    for (uint32_t b = blockIdx.z; b < nb; b += gridDim.z) {
+    for (uint32_t b = blockIdx.z; b < nb; b += gridDim.z)
+    for (uint32_t k0 = blockIdx.y * TT; k0 < ldo; k0 += gridDim.y * TT) {
         const float* s = src + bstride * (int64_t)b;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -828,6 +860,28 @@ uint64_t plane_rows(const Operand& o) { return o.mn_major ? o.inner : o.outer; }
 uint32_t plane_k(const Operand& o) { return (uint32_t)(o.mn_major ? o.outer : o.inner); }
 uint64_t plane_elems(const Operand& o) { return o.nb * plane_rows(o) * rup4(plane_k(o)); }
 
+// True when the registers a thread of this kernel is launched with, times its
+// threads, cover the setmaxnreg split (warpgroup 0 at REGS_LOW, the rest at
+// REGS_HIGH).  A split larger than that allocation would leave the epilogue
+// warps' setmaxnreg.inc waiting forever, so such a kernel is never launched.
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
+bool reg_split_fits() {
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
+    if constexpr (!C_::REG_SPLIT) {
+        return true;
+    } else {
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES, PAIR>) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        const uint64_t have = (uint64_t)((fa.numRegs + 7) & ~7) * C_::THREADS;
+        const uint64_t need = 128ull * C_::REGS_LOW + (uint64_t)(C_::THREADS - 128) * C_::REGS_HIGH;
+        return fa.numRegs > 0 && have >= need;
+    }
+}
+
 // One CTA per SM (persistent over `units` work units), or for PAIR one 2-CTA
 // cluster per pair of SMs, as many clusters as the device can hold at once.
 template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
@@ -840,6 +894,7 @@ cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cuda
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_done.load() & bit)) {
+        if (!reg_split_fits<KIND, A_MN, B_MN, BN, STAGES, PAIR>()) return cudaErrorNotSupported;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)C_::SMEM_BYTES);
         if (e != cudaSuccess) return e;
@@ -861,8 +916,8 @@ cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cuda
             }
             max_clusters[dev & 63] = n;
             if (getenv("VKBLAS_TRACE"))
-                fprintf(stderr, "[vkblas] device %d: %d resident 2-CTA clusters for %s (%d SMs)\n",
-                        dev, n, KIND == K_TF32X3 ? "3xTF32" : "kind::f16", num_sms);
+                fprintf(stderr, "[vkblas] device %d: %d resident 2-CTA clusters for %s, %d-wide tiles (%d SMs)\n",
+                        dev, n, KIND == K_TF32X3 ? "3xTF32" : "kind::f16", BN, num_sms);
         }
         attr_done.fetch_or(bit);
     }
@@ -919,14 +974,32 @@ cudaError_t launch_reduce(const UmmaParams& prm, cudaStream_t s) {
 }
 
 constexpr int BN_16 = 256, STAGES_16 = 4;
+constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
 // CTA pairs (256-row tiles): half of B per CTA leaves room for deeper rings.
 constexpr int STAGES_16P = 6, STAGES_TF32P = 4;
+// 3xTF32 on CTA pairs with 256 x 256 tiles: 64 KB stages (big and small
+// planes of 128 A rows and 128 B rows per CTA).
+constexpr int BN_TF32W = 256, STAGES_TF32W = 3;
 
 // VKBLAS_TC_PAIR=0 keeps every tensor-core GEMM on single-CTA tiles.
 bool pair_enabled() {
     static const bool on = [] {
         const char* e = getenv("VKBLAS_TC_PAIR");
         return !(e && *e && atoi(e) == 0);
+    }();
+    return on;
+}
+
+// 3xTF32 GEMMs on CTA pairs with N >= 256 use 256-wide tiles: each MMA
+// computes twice the columns for the same A tile, which halves the A operand's
+// shared-memory reads and the MMA count per flop (measured on B200 at 4096^3:
+// the GEMM kernel 0.577 -> 0.465 ms).  On with VKBLAS_TF32_WIDE=1.  Taken only
+// when the kernel's register split fits.
+bool tf32_wide() {
+    static const bool on = [] {
+        const char* e = getenv("VKBLAS_TF32_WIDE");
+        return e && *e && atoi(e) != 0 &&
+               reg_split_fits<K_TF32X3, false, false, BN_TF32W, STAGES_TF32W, true>();
     }();
     return on;
 }
@@ -963,10 +1036,10 @@ struct KernelShape {
 KernelShape kernel_shape(const GemmProblem& p) {
     if (small_m_swap(p)) return {swapped(p), true, (uint32_t)BN_SM, false, (uint32_t)BM};
     const bool pair = pair_enabled() && p.M >= 2u * BM;
-    return {p, false, (uint32_t)(p.dtype == DT_F32 ? 128 : BN_16), pair,
-            (uint32_t)(pair ? 2 * BM : BM)};
+    uint32_t bn = p.dtype == DT_F32 ? (uint32_t)BN_TF32 : (uint32_t)BN_16;
+    if (p.dtype == DT_F32 && pair && p.N >= (uint32_t)BN_TF32W && tf32_wide()) bn = BN_TF32W;
+    return {p, false, bn, pair, (uint32_t)(pair ? 2 * BM : BM)};
 }
-constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
 
 // Work decomposition.  Whole waves of tiles run unsplit; the tiles of the
 // last, partial wave (all tiles when there are fewer tiles than SMs -- the
@@ -1056,6 +1129,8 @@ bool umma_uses_pair(const GemmProblem& p, int num_sms, bool split_ws) {
     return kernel_shape(p).pair;
 }
 
+int umma_tile_n(const GemmProblem& p) { return (int)kernel_shape(p).BN; }
+
 int umma_split_count(const GemmProblem& p, int num_sms) {
     return (int)plan_split(kernel_shape(p), num_sms).s;
 }
@@ -1143,7 +1218,8 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
                     reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
                     (uint32_t)o.ld, (int64_t)o.bstride, (uint32_t)o.nb, ldo, big, small);
             } else {
-                dim3 grid((uint32_t)((o.inner + TT - 1) / TT), (uint32_t)((o.outer + TT - 1) / TT),
+                const uint64_t ktiles = (o.outer + TT - 1) / TT;     // the kernel strides beyond
+                dim3 grid((uint32_t)((o.inner + TT - 1) / TT), (uint32_t)(ktiles < 65535 ? ktiles : 65535),
                           (uint32_t)(o.nb < 65535 ? o.nb : 65535));
                 split_tf32_t_kernel<<<grid, 256, 0, s>>>(
                     reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
@@ -1202,8 +1278,10 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
                        : launch_majors<K_BF16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_F32:   // planes are K-major whatever op(A), op(B) are
-            e = pair ? launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32P, true>(prm, units, num_sms, s)
-                     : launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32, false>(prm, units, num_sms, s);
+            e = !pair ? launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32, false>(prm, units, num_sms, s)
+                : BN == BN_TF32W
+                    ? launch_kind<K_TF32X3, false, false, BN_TF32W, STAGES_TF32W, true>(prm, units, num_sms, s)
+                    : launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32P, true>(prm, units, num_sms, s);
             break;
         default: return cudaErrorInvalidValue;
     }
@@ -1220,8 +1298,9 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
                            : launch_reduce<__nv_bfloat16, BN_16>(prm, s);
                 break;
             default:
-                e = pair ? launch_reduce<float, BN_TF32, 2 * BM>(prm, s)
-                         : launch_reduce<float, BN_TF32>(prm, s);
+                e = !pair ? launch_reduce<float, BN_TF32>(prm, s)
+                    : BN == BN_TF32W ? launch_reduce<float, BN_TF32W, 2 * BM>(prm, s)
+                                     : launch_reduce<float, BN_TF32, 2 * BM>(prm, s);
         }
     }
     if (ev_end && e == cudaSuccess) cudaEventRecord(ev_end, s);
