@@ -993,12 +993,12 @@ bool pair_enabled() {
 // 3xTF32 GEMMs on CTA pairs with N >= 256 use 256-wide tiles: each MMA
 // computes twice the columns for the same A tile, which halves the A operand's
 // shared-memory reads and the MMA count per flop (measured on B200 at 4096^3:
-// the GEMM kernel 0.577 -> 0.465 ms).  On with VKBLAS_TF32_WIDE=1.  Taken only
-// when the kernel's register split fits.
+// the GEMM kernel 0.577 -> 0.465 ms).  VKBLAS_TF32_WIDE=0 keeps 128-wide
+// tiles.  Taken only when the kernel's register split fits.
 bool tf32_wide() {
     static const bool on = [] {
         const char* e = getenv("VKBLAS_TF32_WIDE");
-        return e && *e && atoi(e) != 0 &&
+        return !(e && *e && atoi(e) == 0) &&
                reg_split_fits<K_TF32X3, false, false, BN_TF32W, STAGES_TF32W, true>();
     }();
     return on;
