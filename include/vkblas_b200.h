@@ -120,6 +120,32 @@ uint64_t vkblas_b200_launch_count(void);
 /* Library version string. */
 const char* vkblas_b200_version(void);
 
+/* Tile and split plan of a tensor-core GEMM (pure host logic; no device is
+ * touched).  For the engine call (dtype, op_a, op_b, M, N, K, batch) on a
+ * device with `num_sms` SMs it reports the tiles the tcgen05 kernel would run
+ * and how the tiles of the last, partial wave are cut along K.  allow_wide:
+ * whether 256-wide 3xTF32 pair tiles may be chosen (the launch path allows
+ * them when its kernel's register split fits and VKBLAS_TF32_WIDE is not 0).
+ * The plan assumes the K-split is on (VKBLAS_TC_SPLIT) and its scratch can be
+ * had.  Returns VKBLAS_ERR_PARAM for a zero size, num_sms < 1, an unknown dtype
+ * or a null `out`.  No counterpart in the reference. */
+typedef struct {
+    uint32_t tile_m;             /* rows of a tile: 128, or 256 on CTA pairs */
+    uint32_t tile_n;             /* columns of a tile */
+    uint32_t transposed;         /* 1: small-M 2-byte GEMM run as C^T = op(B)^T op(A)^T;
+                                    tile_m, tile_n and tiles then refer to C^T */
+    uint32_t pair;               /* 1: 2-CTA clusters (cta_group::2) */
+    uint32_t tiles;              /* tiles over all batch entries */
+    uint32_t full_tiles;         /* tiles computed whole (the full waves) */
+    uint32_t splits;             /* K ranges each remaining tile is cut into; 1 = none */
+    uint32_t kblocks;            /* k-blocks per tile: K / 32 (fp32) or K / 64, rounded up */
+    uint32_t kblocks_per_split;  /* k-blocks per K range of a split tile */
+    uint64_t partial_bytes;      /* fp32 partial-tile scratch of the split tiles */
+} vkblas_b200_tc_plan_t;
+vkblas_status_t vkblas_b200_tc_plan(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op_t op_b,
+                                    uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
+                                    int num_sms, int allow_wide, vkblas_b200_tc_plan_t* out);
+
 /* Multi-GPU shard planner (pure host logic).  Splits `units` work units
  * (batch entries, or column blocks of `block` columns) into `world` contiguous
  * ranges as evenly as possible; returns this rank's [begin, begin+count).

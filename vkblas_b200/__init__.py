@@ -85,6 +85,8 @@ def _load() -> C.CDLL:
     lib.vkblas_shard_range.argtypes = [C.c_uint64, C.c_uint64, i32, i32,
                                        C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
     lib.vkblas_shard_range.restype = i32
+    lib.vkblas_b200_tc_plan.argtypes = [i32, i32, i32, u32, u32, u32, u32, i32, i32, vp]
+    lib.vkblas_b200_tc_plan.restype = i32
     return lib
 
 
@@ -172,6 +174,24 @@ def release_workspaces(stream=None, all_streams: bool = False) -> None:
 
 def launch_count() -> int:
     return int(_get().vkblas_b200_launch_count())
+
+
+class _TcPlan(C.Structure):
+    _fields_ = [(name, C.c_uint32) for name in (
+        "tile_m", "tile_n", "transposed", "pair", "tiles", "full_tiles", "splits", "kblocks",
+        "kblocks_per_split")] + [("partial_bytes", C.c_uint64)]
+
+
+def tc_plan(dtype: int, op_a: int, op_b: int, M: int, N: int, K: int, batch: int = 1,
+            num_sms: int = 148, allow_wide: bool = True) -> dict:
+    """Tile and split plan of a tensor-core GEMM (vkblas_b200_tc_plan; pure
+    host logic, no GPU needed) as a dict of the struct's fields."""
+    out = _TcPlan()
+    st = _get().vkblas_b200_tc_plan(dtype, op_a, op_b, M, N, K, batch, num_sms,
+                                    1 if allow_wide else 0, C.byref(out))
+    if st != VKBLAS_OK:
+        raise VkblasError(f"vkblas_b200_tc_plan status {st}")
+    return {name: int(getattr(out, name)) for name, _ in _TcPlan._fields_}
 
 
 def shard_range(units: int, rank: int, world: int, block: int = 1):

@@ -90,6 +90,14 @@ int umma_split_count(const GemmProblem& p, int num_sms);   // K splits of the la
 // True when the call runs on 2-CTA clusters (256-row tiles, cta_group::2).
 bool umma_uses_pair(const GemmProblem& p, int num_sms, bool split_ws);
 int umma_tile_n(const GemmProblem& p);                      // N width of the kernel's tile
+// Tile and split plan of a tensor-core GEMM (pure host logic, see
+// vkblas_b200_tc_plan); allow_wide: 256-wide 3xTF32 pair tiles may be chosen.
+struct UmmaPlan {
+    uint32_t tile_m, tile_n, transposed, pair;
+    uint32_t tiles, full_tiles, splits, kblocks, kblocks_per_split;
+    uint64_t partial_bytes;
+};
+UmmaPlan umma_plan(const GemmProblem& p, int num_sms, bool allow_wide);
 // cudaErrorNotSupported: the operands cannot be described to TMA (nothing launched).
 // test_stall: test hook, the producer leaves the first stage empty so the
 // MMA warp's bounded wait runs out (status DS_TIMEOUT_MMA) after 20 ms.

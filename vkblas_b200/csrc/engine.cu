@@ -570,6 +570,30 @@ VKB_EXPORT uint64_t vkblas_b200_launch_count(void) { return g_launches.load(); }
 
 VKB_EXPORT const char* vkblas_b200_version(void) { return "vkblas-b200 0.1 (sm_100a)"; }
 
+VKB_EXPORT vkblas_status_t vkblas_b200_tc_plan(vkblas_dtype_t dtype, vkblas_op_t op_a,
+                                               vkblas_op_t op_b, uint32_t M, uint32_t N,
+                                               uint32_t K, uint32_t batch, int num_sms,
+                                               int allow_wide, vkblas_b200_tc_plan_t* out) {
+    if (!out || !M || !N || !K || !batch || num_sms < 1) return VKBLAS_ERR_PARAM;
+    if (dtype != VKBLAS_DT_F32 && dtype != VKBLAS_DT_F16 && dtype != VKBLAS_DT_BF16)
+        return VKBLAS_ERR_PARAM;
+    // Only sizes, types and ops shape the plan; pointers and leading dimensions do not.
+    GemmProblem p = make_problem((int)dtype, op_a, op_b, M, N, K, 1.f, nullptr, 0, nullptr, 0, 0.f,
+                                 nullptr, 0, batch, 0, 0, 0);
+    const UmmaPlan r = umma_plan(p, num_sms, allow_wide != 0);
+    out->tile_m = r.tile_m;
+    out->tile_n = r.tile_n;
+    out->transposed = r.transposed;
+    out->pair = r.pair;
+    out->tiles = r.tiles;
+    out->full_tiles = r.full_tiles;
+    out->splits = r.splits;
+    out->kblocks = r.kblocks;
+    out->kblocks_per_split = r.kblocks_per_split;
+    out->partial_bytes = r.partial_bytes;
+    return VKBLAS_OK;
+}
+
 VKB_EXPORT vkblas_status_t vkblas_shard_range(uint64_t units, uint64_t block, int rank, int world,
                                               uint64_t* begin, uint64_t* count) {
     if (world < 1 || rank < 0 || rank >= world || !begin || !count) return VKBLAS_ERR_PARAM;

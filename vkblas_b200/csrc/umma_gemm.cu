@@ -1033,13 +1033,16 @@ struct KernelShape {
     bool pair;
     uint32_t bm_tile;
 };
-KernelShape kernel_shape(const GemmProblem& p) {
+// `wide`: whether 256-wide 3xTF32 pair tiles may be chosen (tf32_wide() on the
+// launch path).
+KernelShape kernel_shape(const GemmProblem& p, bool wide) {
     if (small_m_swap(p)) return {swapped(p), true, (uint32_t)BN_SM, false, (uint32_t)BM};
     const bool pair = pair_enabled() && p.M >= 2u * BM;
     uint32_t bn = p.dtype == DT_F32 ? (uint32_t)BN_TF32 : (uint32_t)BN_16;
-    if (p.dtype == DT_F32 && pair && p.N >= (uint32_t)BN_TF32W && tf32_wide()) bn = BN_TF32W;
+    if (p.dtype == DT_F32 && pair && p.N >= (uint32_t)BN_TF32W && wide) bn = BN_TF32W;
     return {p, false, bn, pair, (uint32_t)(pair ? 2 * BM : BM)};
 }
+KernelShape kernel_shape(const GemmProblem& p) { return kernel_shape(p, tf32_wide()); }
 
 // Work decomposition.  Whole waves of tiles run unsplit; the tiles of the
 // last, partial wave (all tiles when there are fewer tiles than SMs -- the
@@ -1130,6 +1133,25 @@ bool umma_uses_pair(const GemmProblem& p, int num_sms, bool split_ws) {
 }
 
 int umma_tile_n(const GemmProblem& p) { return (int)kernel_shape(p).BN; }
+
+UmmaPlan umma_plan(const GemmProblem& p, int num_sms, bool allow_wide) {
+    const KernelShape ks = kernel_shape(p, allow_wide);
+    const SplitPlan pl = plan_split(ks, num_sms);
+    const GemmProblem& q = ks.q;
+    const uint32_t bk = ROW_BYTES / (q.dtype == DT_F32 ? 4u : 2u);
+    UmmaPlan r;
+    r.tile_m = ks.bm_tile;
+    r.tile_n = ks.BN;
+    r.transposed = ks.c_trans ? 1u : 0u;
+    r.pair = ks.pair ? 1u : 0u;
+    r.tiles = pl.s > 1 ? pl.full + (pl.units - pl.full) / pl.s : pl.units;
+    r.full_tiles = pl.full;
+    r.splits = pl.s;
+    r.kblocks = (q.K + bk - 1) / bk;
+    r.kblocks_per_split = pl.kb_per;
+    r.partial_bytes = pl.s > 1 ? (uint64_t)pl.partial_bytes : 0u;
+    return r;
+}
 
 int umma_split_count(const GemmProblem& p, int num_sms) {
     return (int)plan_split(kernel_shape(p), num_sms).s;
