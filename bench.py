@@ -298,6 +298,51 @@ def sharded_config5(vk, torch, dist, rank, world, stream):
     return out
 
 
+def _roofline(path, tile_n, pair, split, gemm_ms, ms_step, peaks, peaks_kind):
+    """The bench line's `roofline` object for the headline GEMM kernel: its
+    useful FLOP/s against the peak derived from the measured bf16 burst (and
+    the nominal dense tf32 bound), the tile configuration that ran, and its ncu
+    DRAM traffic where a capture of that configuration is committed."""
+    kernel_tflops = FLOP_PER_GEMM / (ms_step / 1e3) / 1e12
+    gemm_tflops = FLOP_PER_GEMM / (gemm_ms / 1e3) / 1e12
+    traffic, traffic_src = None, None
+    nominal = None
+    if path == "tc":
+        tiles = f"{256 if pair else 128}x{tile_n} tiles" + (" on CTA pairs" if pair else "")
+        kernel_name = f"3xTF32 tcgen05 SGEMM (umma_gemm_kernel, {tiles}" + (
+            f"; last wave split {split} ways, then split_reduce_kernel)" if split > 1 else ")")
+        peak = peaks["bf16_tflops"] / 2.0 / 3.0
+        peak_note = (f"{peaks_kind} bf16 burst {peaks['bf16_tflops']} TF / 2 (TF32 rate) / 3 "
+                     "(three TF32 MMAs per useful FLOP)")
+        # The measured bf16 burst is cuBLAS's own rate, not the hardware's; the
+        # nominal dense tf32 rate / 3 bounds the kernel from above.
+        nominal = {"peak": round(1100.0 / 3.0, 1), "frac": round(gemm_tflops / (1100.0 / 3.0), 4),
+                   "source": "nominal dense tf32 1.1 PFLOP/s / 3"}
+        if pair and tile_n == 128:
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel
+            # at this shape (859.3 MB + 64.1 MB), from the committed ncu capture
+            traffic = 923.4e6
+            traffic_src = "ncu --set full, profiles/umma_gemm_tf32x3_sgemm_nn_4096.md"
+        else:
+            traffic_src = "no ncu capture of this tile configuration"
+    else:
+        kernel_name = "FFMA SIMT SGEMM"
+        peak = 148 * 128 * 2 * (peaks.get("sm_max_mhz", 1965.0) * 1e6) / 1e12
+        peak_note = "FP32 SIMT nominal: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
+    roof = {"bound": "tensor", "kernel": kernel_name, "achieved": round(gemm_tflops, 2),
+            "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(gemm_tflops / peak, 4),
+            "kernel_ms": round(gemm_ms, 4),
+            "achieved_note": "2*4096^3 FLOP per launch / the GEMM kernel's mean duration "
+                             "(CUDA events around it, every timed step); the whole step "
+                             "(split pre-pass + GEMM) runs at step_achieved",
+            "step_achieved": round(kernel_tflops, 2),
+            "peak_source": peak_note, "traffic": traffic, "traffic_unit": "bytes per launch",
+            "traffic_source": traffic_src}
+    if nominal is not None:
+        roof["nominal"] = nominal
+    return roof
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -404,7 +449,6 @@ def main() -> int:
         ms_total, gemm_ms = float(t[0].item()), float(t[1].item())
     ms_step = ms_total / args.steps
     value = world * FLOP_PER_GEMM * args.steps / (ms_total / 1e3) / 1e12
-    kernel_tflops = FLOP_PER_GEMM / (ms_step / 1e3) / 1e12
 
     # e2e through the public ABI with host buffers: every step copies its A and
     # B from pinned host memory, calls hipblasSgemm and copies its C back, all
@@ -461,42 +505,7 @@ def main() -> int:
         e2e_ms = float(t.item())
     e2e_val = world * FLOP_PER_GEMM / (e2e_ms / 1e3) / 1e12
 
-    gemm_tflops = FLOP_PER_GEMM / (gemm_ms / 1e3) / 1e12
-    traffic, traffic_src = None, None
-    nominal = None
-    if path == "tc":
-        tiles = f"{256 if pair else 128}x{tile_n} tiles" + (" on CTA pairs" if pair else "")
-        kernel_name = f"3xTF32 tcgen05 SGEMM (umma_gemm_kernel, {tiles}" + (
-            f"; last wave split {split} ways, then split_reduce_kernel)" if split > 1 else ")")
-        peak = peaks["bf16_tflops"] / 2.0 / 3.0
-        peak_note = (f"{peaks_kind} bf16 burst {peaks['bf16_tflops']} TF / 2 (TF32 rate) / 3 "
-                     "(three TF32 MMAs per useful FLOP)")
-        # The measured bf16 burst is cuBLAS's own rate, not the hardware's; the
-        # nominal dense tf32 rate / 3 bounds the kernel from above.
-        nominal = {"peak": round(1100.0 / 3.0, 1), "frac": round(gemm_tflops / (1100.0 / 3.0), 4),
-                   "source": "nominal dense tf32 1.1 PFLOP/s / 3"}
-        if pair and tile_n == 128:
-            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel
-            # at this shape (859.3 MB + 64.1 MB), from the committed ncu capture
-            traffic = 923.4e6
-            traffic_src = "ncu --set full, profiles/umma_gemm_tf32x3_sgemm_nn_4096.md"
-        else:
-            traffic_src = "no ncu capture of this tile configuration"
-    else:
-        kernel_name = "FFMA SIMT SGEMM"
-        peak = 148 * 128 * 2 * (peaks.get("sm_max_mhz", 1965.0) * 1e6) / 1e12
-        peak_note = "FP32 SIMT nominal: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
-    roof = {"bound": "tensor", "kernel": kernel_name, "achieved": round(gemm_tflops, 2),
-            "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(gemm_tflops / peak, 4),
-            "kernel_ms": round(gemm_ms, 4),
-            "achieved_note": "2*4096^3 FLOP per launch / the GEMM kernel's mean duration "
-                             "(CUDA events around it, every timed step); the whole step "
-                             "(split pre-pass + GEMM) runs at step_achieved",
-            "step_achieved": round(kernel_tflops, 2),
-            "peak_source": peak_note, "traffic": traffic, "traffic_unit": "bytes per launch",
-            "traffic_source": traffic_src}
-    if nominal is not None:
-        roof["nominal"] = nominal
+    roof = _roofline(path, tile_n, pair, split, gemm_ms, ms_step, peaks, peaks_kind)
 
     result = {
         "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,

@@ -25,3 +25,32 @@ def test_reference_arm_json_line():
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "TFLOPS", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+def test_roofline_object_for_each_kernel_configuration():
+    """The GPU arm's `roofline` object (built after the timed region, so a
+    mistake there would cost the whole bench line) for the tile
+    configurations the headline can run on: 256x256 pair tiles with a split
+    last wave, 256x128 pair tiles (whose ncu traffic is committed), and the
+    exact FFMA kernel."""
+    sys.path.insert(0, ROOT)
+    import bench
+    peaks = {"hbm_gbs": 6552.0, "bf16_tflops": 1664.6, "sm_max_mhz": 1965.0}
+    flop = 2.0 * 4096 ** 3
+    gemm_ms, step_ms = 0.465, 0.548
+    wide = bench._roofline("tc", 256, True, 2, gemm_ms, step_ms, peaks, "measured")
+    assert wide["kernel"] == ("3xTF32 tcgen05 SGEMM (umma_gemm_kernel, 256x256 tiles on CTA "
+                              "pairs; last wave split 2 ways, then split_reduce_kernel)")
+    assert abs(wide["achieved"] - flop / gemm_ms / 1e9) < 0.01
+    assert abs(wide["peak"] - 1664.6 / 6) < 0.01
+    assert abs(wide["frac"] - wide["achieved"] / wide["peak"]) < 1e-3
+    assert abs(wide["step_achieved"] - flop / step_ms / 1e9) < 0.01
+    assert wide["traffic"] is None and wide["bound"] == "tensor" and wide["unit"] == "TFLOP/s"
+    assert wide["nominal"]["peak"] == round(1100 / 3, 1) and 0 < wide["nominal"]["frac"] < 1
+    narrow = bench._roofline("tc", 128, True, 1, 0.577, 0.658, peaks, "measured")
+    assert narrow["kernel"].endswith("256x128 tiles on CTA pairs)")
+    assert narrow["traffic"] == 923.4e6
+    ffma = bench._roofline("simt", 0, False, 1, 3.7, 3.7, peaks, "measured")
+    assert ffma["kernel"] == "FFMA SIMT SGEMM" and "nominal" not in ffma
+    assert abs(ffma["peak"] - 148 * 128 * 2 * 1.965e-3) < 0.01
+    json.dumps(wide)
