@@ -363,12 +363,12 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                             if constexpr (PAIR) tma_load_3d_pair(dst, m, fb, c0, c1, c2);
                             else tma_load_3d(dst, m, fb, c0, c1, c2);
                         };
-    #pragma unroll
+#pragma unroll
                         for (int pl = 0; pl < C_::PLANES; pl++) {
                             if (!A_MN) {
                                 load(sA + pl * C_::A_PLANE, &p.tmA[pl], k0, m0, ba);
                             } else {
-    #pragma unroll
+#pragma unroll
                                 for (int j = 0; j < BM / C_::EPB; j++)
                                     load(sA + pl * C_::A_PLANE + j * C_::SLAB, &p.tmA[pl],
                                          m0 + j * C_::EPB, k0, ba);
@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                             if (!B_MN) {
                                 load(sB + pl * C_::B_PLANE, &p.tmB[pl], k0, n0, bb);
                             } else {
-    #pragma unroll
+#pragma unroll
                                 for (int j = 0; j < C_::BNC / C_::EPB; j++)
                                     load(sB + pl * C_::B_PLANE + j * C_::SLAB, &p.tmB[pl],
                                          n0 + j * C_::EPB, k0, bb);
@@ -428,10 +428,10 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                             tc_fence_after();
                             const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
                             const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
-    #pragma unroll
+#pragma unroll
                             for (int j = 0; j < C_::KSTEPS; j++) {
                                 uint64_t ad[C_::PLANES], bd[C_::PLANES];
-    #pragma unroll
+#pragma unroll
                                 for (int pl = 0; pl < C_::PLANES; pl++) {
                                     ad[pl] = A_MN ? smem_desc_sw128(sA + pl * C_::A_PLANE + j * C_::UK * ROW_BYTES,
                                                                     C_::SLAB, 1024)
