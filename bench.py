@@ -159,8 +159,12 @@ def _time_loop(fn, iters, stream):
     return e0.elapsed_time(e1) / iters
 
 
-def secondary_results(vk, hb, torch, peaks):
-    """Other BASELINE configs on one GPU (device-resident inputs, CUDA events)."""
+def secondary_results(vk, hb, torch, peaks, ceil=None):
+    """Other BASELINE configs on one GPU (device-resident inputs, CUDA events).
+    Fractions are of MEASURED_PEAKS.json (bf16 burst, HBM copy) and of the
+    ceilings measured in this run (``ceil``, run_peaks) where one applies."""
+    ceil = ceil or {}
+    f16_ceil = ceil.get("tcgen05_f16_pair", {}).get("tflops")
     out = {}
     s = torch.cuda.Stream()         # CUDA graphs cannot be captured on the default stream
     al, be = hb.fptr(1.0), hb.fptr(0.0)
@@ -182,7 +186,7 @@ def secondary_results(vk, hb, torch, peaks):
         try:
             for i in range(3):
                 run_ffma(i)
-            ms = _time_loop(run_ffma, 6, s)
+            ms = _time_loop(run_ffma, 10, s)
             path = vk.PATH_NAMES[vk.last_path()]
         finally:
             vk.set_path(vk.PATH_AUTO)
@@ -190,6 +194,9 @@ def secondary_results(vk, hb, torch, peaks):
         nominal = 148 * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
         out["sgemm_ffma_nn_4096"] = {"tflops": round(tf, 2), "ms": round(ms, 4), "path": path,
                                      "frac_of_fp32_nominal": round(tf / nominal, 4)}
+        if "ffma_fp32" in ceil:
+            out["sgemm_ffma_nn_4096"]["frac_of_ffma_measured"] = round(
+                tf / ceil["ffma_fp32"]["tflops"], 4)
         del sets
         # config 3: HGEMM T/N 4096^3, 8192^3 and 16384^3
         for n in (4096, 8192, 16384):
@@ -205,11 +212,13 @@ def secondary_results(vk, hb, torch, peaks):
                                         vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
             for i in range(3):
                 run(i)
-            ms = _time_loop(run, {4096: 10, 8192: 4, 16384: 2}[n], s)
+            ms = _time_loop(run, {4096: 20, 8192: 10, 16384: 5}[n], s)
             tf = 2.0 * n ** 3 / ms / 1e9
             out[f"hgemm_tn_{n}"] = {"tflops": round(tf, 2), "ms": round(ms, 4),
                                     "path": vk.PATH_NAMES[vk.last_path()],
                                     "frac_of_bf16_burst": round(tf / peaks["bf16_tflops"], 4)}
+            if f16_ceil:
+                out[f"hgemm_tn_{n}"]["frac_of_f16_mma_measured"] = round(tf / f16_ceil, 4)
             del sets
         # config 4: decode GEMV, 4 rotating weight sets (470 MB > L2).  Timed two
         # ways: back-to-back calls (includes each call's launch gap) and a CUDA
@@ -255,11 +264,13 @@ def secondary_results(vk, hb, torch, peaks):
                 n * n, B.data_ptr(), vk.HIP_R_16F, n, n * n, be, C.data_ptr(), vk.HIP_R_16F, n,
                 n * n, b, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
         run(0)
-        ms = _time_loop(run, 3, s)
+        ms = _time_loop(run, 10, s)
         tf = 256 * 2.0 * n ** 3 / ms / 1e9
         out["hgemm_batched_256x2048"] = {"tflops": round(tf, 2), "ms": round(ms, 3),
                                          "path": vk.PATH_NAMES[vk.last_path()],
                                          "frac_of_bf16_burst": round(tf / peaks["bf16_tflops"], 4)}
+        if f16_ceil:
+            out["hgemm_batched_256x2048"]["frac_of_f16_mma_measured"] = round(tf / f16_ceil, 4)
         del A, B, C
     return out
 
@@ -298,37 +309,234 @@ def sharded_config5(vk, torch, dist, rank, world, stream):
     return out
 
 
-def _roofline(path, tile_n, pair, split, gemm_ms, ms_step, peaks, peaks_kind):
+# ------------------------------------------------------- single-case runner
+CASES = ["sgemm", "sgemm-simt", "hgemm", "gemv", "gemv32", "batched", "dgemm", "zgemm", "peaks"]
+
+
+def run_peaks(vk, torch, stream, reps=3):
+    """Throughput ceilings of this GPU (vkblas_b200_peak_launch): each kernel
+    once untimed, then `reps` launches timed with CUDA events; TFLOP/s of the
+    best.  Sized to about 2 ms a launch."""
+    import ctypes as C
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    iters = {0: 2048, 1: 8192, 2: 8192, 3: 8192, 4: 8192}
+    names = {0: "ffma_fp32", 1: "tcgen05_tf32", 2: "tcgen05_tf32_pair", 3: "tcgen05_f16",
+             4: "tcgen05_f16_pair"}
+    out = {}
+    for which, name in names.items():
+        flops = C.c_double()
+        ms = []
+        for r in range(reps + 1):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            st = vk.lib.vkblas_b200_peak_launch(which, iters[which], stream.cuda_stream,
+                                                status.data_ptr(), C.byref(flops))
+            e1.record(stream)
+            if st != vk.VKBLAS_OK:
+                raise RuntimeError(f"vkblas_b200_peak_launch({which}) status {st}")
+            torch.cuda.synchronize()
+            if r:
+                ms.append(e0.elapsed_time(e1))
+        if int(status.item()) != 0:
+            raise RuntimeError(f"peak kernel {name}: device status {int(status.item())}")
+        out[name] = {"tflops": round(flops.value / min(ms) / 1e9, 1), "ms": round(min(ms), 4)}
+    return out
+
+
+def run_case(a) -> int:
+    """One GEMM case of the BASELINE configs, `--iters` times on torch's current
+    stream after one untimed call (for timing and ncu captures):
+
+        python bench.py --case sgemm  [--n 4096] [--shape M,N,K]   # 3xTF32, N/N
+        python bench.py --case sgemm-simt [--n 4096]               # exact FFMA kernel
+        python bench.py --case hgemm  [--n 4096] [--shape M,N,K]   # fp16 tcgen05, hipBLAS T/N
+        python bench.py --case gemv   [--m 1] [--splitk 4]         # decode, K=4096, N=14336
+        python bench.py --case gemv32 [--m 1] [--trans t|n]        # fp32 decode
+        python bench.py --case dgemm|zgemm [--n 2048]              # fp64 / complex128 N/N
+        python bench.py --case batched                             # 256 x 2048^3 fp16 N/N
+        python bench.py --case peaks                               # tcgen05 / FFMA ceilings
+
+    Inputs are device-resident and seeded; the mean time per call (CUDA
+    events) is printed.  --path simt|tc|gemv forces a kernel family."""
+    import torch
+    import vkblas_b200 as vk
+    from vkblas_b200 import hipblas as hb
+
+    if a.case == "peaks":
+        torch.cuda.init()
+        s = torch.cuda.current_stream()
+        with ClockSampler(torch.cuda.current_device(), period_s=0.005) as clk:
+            res = run_peaks(vk, torch, s, reps=max(1, a.iters))
+        res["clocks"] = clk.summary()
+        print(json.dumps(res))
+        return 0
+    torch.cuda.init()
+    s = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    h = hb.Handle()
+    h.set_stream(s)
+    n = a.n
+    M, N, K = (int(x) for x in a.shape.split(",")) if a.shape else (n, n, n)
+    if a.case in ("sgemm", "sgemm-simt"):
+        A = torch.randn(M * K, device="cuda", generator=g)
+        B = torch.randn(K * N, device="cuda", generator=g)
+        C = torch.empty(M * N, device="cuda")
+        if a.case == "sgemm-simt":
+            vk.set_path(vk.PATH_SIMT)
+        flop, nbytes = 2.0 * M * N * K, 0.0
+        # column-major C (M x N) = A (M x K) * B (K x N)
+        call = lambda: vk.lib.hipblasSgemm(h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, M, N, K, al,  # noqa: E731
+                                           A.data_ptr(), M, B.data_ptr(), K, be, C.data_ptr(), M)
+    elif a.case == "hgemm":
+        A = (torch.randn(M * K, device="cuda", generator=g) * 0.02).half()
+        B = (torch.randn(K * N, device="cuda", generator=g) * 0.02).half()
+        C = torch.empty(M * N, device="cuda", dtype=torch.float16)
+        flop, nbytes = 2.0 * M * N * K, 0.0
+        # column-major C (M x N) = A^T (A stored K x M) * B (K x N)
+        call = lambda: vk.lib.hipblasGemmEx_v2(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, M, N, K, al,  # noqa: E731
+                                               A.data_ptr(), vk.HIP_R_16F, K, B.data_ptr(),
+                                               vk.HIP_R_16F, K, be, C.data_ptr(), vk.HIP_R_16F, M,
+                                               vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+    elif a.case == "gemv":
+        K, O, M = 4096, 14336, a.m
+        # four weight sets (470 MB > 126 MB L2), rotated call by call
+        Ws = [(torch.randn(O * K, device="cuda", generator=g) * 0.02).half() for _ in range(4)]
+        X = torch.randn(M * K, device="cuda", generator=g).half()
+        C = torch.empty(M * O, device="cuda", dtype=torch.float16)
+        if a.splitk:
+            vk.set_splitk(a.splitk)
+        flop, nbytes = 2.0 * M * O * K, 2.0 * (O * K + M * K + M * O)
+        turn = [0]
+
+        def call():
+            turn[0] += 1
+            return vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,
+                                        Ws[turn[0] % 4].data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
+                                        vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F, O,
+                                        vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+    elif a.case == "gemv32":
+        K, O, M = 4096, 14336, a.m
+        # four fp32 weight sets (940 MB > 126 MB L2), rotated call by call
+        Ws = [torch.randn(O * K, device="cuda", generator=g) * 0.02 for _ in range(4)]
+        X = torch.randn(M * K, device="cuda", generator=g)
+        C = torch.empty(M * O, device="cuda")
+        if a.splitk:
+            vk.set_splitk(a.splitk)
+        flop, nbytes = 2.0 * M * O * K, 4.0 * (O * K + M * K + M * O)
+        tA = vk.HIPBLAS_OP_T if a.trans == "t" else vk.HIPBLAS_OP_N
+        lda = K if a.trans == "t" else O
+        turn = [0]
+
+        def call():
+            turn[0] += 1
+            return vk.lib.hipblasSgemm(h.h, tA, vk.HIPBLAS_OP_N, O, M, K, al,
+                                       Ws[turn[0] % 4].data_ptr(), lda, X.data_ptr(), K, be,
+                                       C.data_ptr(), O)
+    elif a.case in ("dgemm", "zgemm"):
+        cplx = a.case == "zgemm"
+        w = 2 if cplx else 1
+        A = torch.randn(w * M * K, device="cuda", generator=g, dtype=torch.float64)
+        B = torch.randn(w * K * N, device="cuda", generator=g, dtype=torch.float64)
+        C = torch.zeros(w * M * N, device="cuda", dtype=torch.float64)
+        vk.set_stream(s)
+        # useful FLOP: a complex multiply-add is 4 real ones
+        flop, nbytes = (8.0 if cplx else 2.0) * M * N * K, 0.0
+        if cplx:
+            call = lambda: vk.lib.vkblas_gemm_z64(0, 0, M, N, K, 1.0, 0.0, A.data_ptr(), K,  # noqa: E731
+                                                  B.data_ptr(), N, 0.0, 0.0, C.data_ptr(), N, 1,
+                                                  0, 0, 0)
+        else:
+            call = lambda: vk.lib.vkblas_gemm_f64(0, 0, M, N, K, 1.0, A.data_ptr(), K,  # noqa: E731
+                                                  B.data_ptr(), N, 0.0, C.data_ptr(), N, 1, 0, 0, 0)
+    else:
+        b, n = 256, 2048
+        A = (torch.randn(b * n * n, device="cuda", generator=g) * 0.02).half()
+        B = (torch.randn(b * n * n, device="cuda", generator=g) * 0.02).half()
+        C = torch.empty(b * n * n, device="cuda", dtype=torch.float16)
+        flop, nbytes = b * 2.0 * n ** 3, 0.0
+        call = lambda: vk.lib.hipblasGemmStridedBatchedEx_v2(  # noqa: E731
+            h.h, vk.HIPBLAS_OP_N, vk.HIPBLAS_OP_N, n, n, n, al, A.data_ptr(), vk.HIP_R_16F, n,
+            n * n, B.data_ptr(), vk.HIP_R_16F, n, n * n, be, C.data_ptr(), vk.HIP_R_16F, n, n * n,
+            b, vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+
+    if a.path != "auto":
+        vk.set_path({"simt": vk.PATH_SIMT, "tc": vk.PATH_TC, "gemv": vk.PATH_GEMV}[a.path])
+    st = call()
+    if st != 0:
+        raise SystemExit(f"status {st}")
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(a.iters):
+        call()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(1, a.iters)
+    st = vk.device_status(True)
+    line = f"{a.case}: {ms * 1e3:.2f} us/call, {flop / ms / 1e9:.2f} TFLOP/s"
+    if nbytes:
+        line += f", {nbytes / ms / 1e6:.1f} GB/s"
+    print(line + f", path={vk.PATH_NAMES[vk.last_path()]}, status={st}")
+    h.close()
+    return 0 if st == 0 else 1
+
+
+
+def _roofline(path, tile_n, pair, split, gemm_ms, ms_step, peaks, peaks_kind, ceil=None):
     """The bench line's `roofline` object for the headline GEMM kernel: its
-    useful FLOP/s against the peak derived from the measured bf16 burst (and
-    the nominal dense tf32 bound), the tile configuration that ran, and its ncu
-    DRAM traffic where a capture of that configuration is committed."""
+    useful FLOP/s against the ceiling measured in the same run (``ceil``, from
+    run_peaks: the tcgen05 kind::tf32 MMA loop / 3, or the FFMA loop), with the
+    peak derived from MEASURED_PEAKS.json's bf16 burst beside it, the tile
+    configuration that ran, and its ncu DRAM traffic per launch where a capture
+    of that configuration is committed under profiles/."""
     kernel_tflops = FLOP_PER_GEMM / (ms_step / 1e3) / 1e12
     gemm_tflops = FLOP_PER_GEMM / (gemm_ms / 1e3) / 1e12
     traffic, traffic_src = None, None
-    nominal = None
+    extra = {}
     if path == "tc":
         tiles = f"{256 if pair else 128}x{tile_n} tiles" + (" on CTA pairs" if pair else "")
         kernel_name = f"3xTF32 tcgen05 SGEMM (umma_gemm_kernel, {tiles}" + (
             f"; last wave split {split} ways, then split_reduce_kernel)" if split > 1 else ")")
-        peak = peaks["bf16_tflops"] / 2.0 / 3.0
-        peak_note = (f"{peaks_kind} bf16 burst {peaks['bf16_tflops']} TF / 2 (TF32 rate) / 3 "
-                     "(three TF32 MMAs per useful FLOP)")
-        # The measured bf16 burst is cuBLAS's own rate, not the hardware's; the
-        # nominal dense tf32 rate / 3 bounds the kernel from above.
-        nominal = {"peak": round(1100.0 / 3.0, 1), "frac": round(gemm_tflops / (1100.0 / 3.0), 4),
-                   "source": "nominal dense tf32 1.1 PFLOP/s / 3"}
-        if pair and tile_n == 128:
-            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel
-            # at this shape (859.3 MB + 64.1 MB), from the committed ncu capture
+        derived = peaks["bf16_tflops"] / 2.0 / 3.0
+        key = "tcgen05_tf32_pair" if pair else "tcgen05_tf32"
+        if ceil and key in ceil:
+            peak = ceil[key]["tflops"] / 3.0
+            peak_note = (f"measured in this run: tcgen05.mma kind::tf32 loop on every SM "
+                         f"({key}, bench.py --case peaks) {ceil[key]['tflops']} TF / 3 "
+                         "(three TF32 MMAs per useful FLOP)")
+        else:
+            peak = derived
+            peak_note = (f"{peaks_kind} bf16 burst {peaks['bf16_tflops']} TF / 2 (TF32 rate) / 3 "
+                         "(three TF32 MMAs per useful FLOP)")
+        # cuBLAS's own bf16 rate, not the hardware's, halved for tf32
+        extra["cublas_derived"] = {"peak": round(derived, 2), "frac": round(gemm_tflops / derived, 4),
+                                   "source": f"{peaks_kind} bf16 burst {peaks['bf16_tflops']} TF "
+                                             "/ 2 / 3"}
+        extra["nominal"] = {"peak": round(1100.0 / 3.0, 1),
+                            "frac": round(gemm_tflops / (1100.0 / 3.0), 4),
+                            "source": "nominal dense tf32 1.1 PFLOP/s / 3"}
+        # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel
+        # at 4096^3, from the committed ncu captures
+        if pair and tile_n == 256:
+            traffic = 695.2e6
+            traffic_src = "ncu --set full, profiles/umma_gemm_tf32x3_256x256_sgemm_nn_4096.md"
+        elif pair and tile_n == 128:
             traffic = 923.4e6
-            traffic_src = "ncu --set full, profiles/umma_gemm_tf32x3_sgemm_nn_4096.md"
+            traffic_src = "ncu --set full, profiles/umma_gemm_tf32x3_256x128_sgemm_nn_4096.md"
         else:
             traffic_src = "no ncu capture of this tile configuration"
+        extra["algorithmic_bytes"] = 4 * 4096 * 4096 * 4 + 4096 * 4096 * 4
     else:
         kernel_name = "FFMA SIMT SGEMM"
-        peak = 148 * 128 * 2 * (peaks.get("sm_max_mhz", 1965.0) * 1e6) / 1e12
-        peak_note = "FP32 SIMT nominal: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
+        if ceil and "ffma_fp32" in ceil:
+            peak = ceil["ffma_fp32"]["tflops"]
+            peak_note = "measured in this run: FFMA loop on every SM (bench.py --case peaks)"
+        else:
+            peak = 148 * 128 * 2 * (peaks.get("sm_max_mhz", 1965.0) * 1e6) / 1e12
+            peak_note = "FP32 SIMT nominal: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
     roof = {"bound": "tensor", "kernel": kernel_name, "achieved": round(gemm_tflops, 2),
             "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(gemm_tflops / peak, 4),
             "kernel_ms": round(gemm_ms, 4),
@@ -338,8 +546,7 @@ def _roofline(path, tile_n, pair, split, gemm_ms, ms_step, peaks, peaks_kind):
             "step_achieved": round(kernel_tflops, 2),
             "peak_source": peak_note, "traffic": traffic, "traffic_unit": "bytes per launch",
             "traffic_source": traffic_src}
-    if nominal is not None:
-        roof["nominal"] = nominal
+    roof.update(extra)
     return roof
 
 
@@ -353,7 +560,19 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=60.0,
                     help="--impl reference: host CPU time to spend over all timed steps")
+    ap.add_argument("--case", choices=CASES, help="run one case (see run_case) and exit")
+    ap.add_argument("--trans", default="t", choices=["t", "n"],
+                    help="--case gemv32: hipBLAS transA of the weights (t: N x K rows, n: K x N)")
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--shape", default="", help="--case: M,N,K (default n,n,n)")
+    ap.add_argument("--m", type=int, default=1, help="--case gemv/gemv32: tokens")
+    ap.add_argument("--splitk", type=int, default=0)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc", "gemv"],
+                    help="--case: force a kernel family (vkblas_b200_set_path)")
     args = ap.parse_args()
+    if args.case:
+        return run_case(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -429,7 +648,7 @@ def main() -> int:
     l0 = vk.launch_count()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, period_s=0.005) as clk:
         e0.record(stream)
         for i in range(args.steps):
             vk.set_kernel_events(*kev[i])
@@ -505,7 +724,14 @@ def main() -> int:
         e2e_ms = float(t.item())
     e2e_val = world * FLOP_PER_GEMM / (e2e_ms / 1e3) / 1e12
 
-    roof = _roofline(path, tile_n, pair, split, gemm_ms, ms_step, peaks, peaks_kind)
+    # Ceilings of this GPU measured now (tcgen05 tf32 / f16 MMA loops, FFMA
+    # loop; about 50 ms): the roofline's denominators.
+    try:
+        ceil = run_peaks(vk, torch, stream)
+    except Exception as exc:      # the derived peaks stand in; the error is reported
+        ceil = {"error": repr(exc)}
+    roof = _roofline(path, tile_n, pair, split, gemm_ms, ms_step, peaks, peaks_kind,
+                     ceil if "error" not in ceil else None)
 
     result = {
         "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,
@@ -525,6 +751,7 @@ def main() -> int:
                               "the previous step's GEMM and D2H copy"},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
+        "measured_ceilings": ceil,
     }
     del sets, hA, hB, hCs
     torch.cuda.empty_cache()
@@ -533,7 +760,8 @@ def main() -> int:
         result["cpu_baseline"] = dict(value=tf, unit="TFLOPS", **info)
     if rank == 0 and world == 1 and not args.no_secondary:
         try:
-            result["secondary"] = secondary_results(vk, hb, torch, peaks)
+            result["secondary"] = secondary_results(vk, hb, torch, peaks,
+                                                    ceil if "error" not in ceil else None)
         except Exception as exc:   # secondary numbers never hide the headline
             result["secondary"] = {"error": repr(exc)}
     if world > 1 and not args.no_secondary:

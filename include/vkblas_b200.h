@@ -146,6 +146,25 @@ vkblas_status_t vkblas_b200_tc_plan(vkblas_dtype_t dtype, vkblas_op_t op_a, vkbl
                                     uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
                                     int num_sms, int allow_wide, vkblas_b200_tc_plan_t* out);
 
+/* Throughput microbenchmarks of the current device (no counterpart in the
+ * reference's API; its test/fma_peak.c measured its FMA ceiling the same way).
+ * Enqueues one launch of kernel `which` on `stream` (a cudaStream_t) that
+ * runs `iters` rounds of only the instruction under test on every SM, and
+ * stores the FLOP that launch performs in *flops; the caller times it with
+ * CUDA events.  `status` is a device int that a bounded wait sets non-zero
+ * if the tensor core's final commit never arrived.  VKBLAS_ERR_PARAM for an
+ * unknown `which`, iters == 0 or null pointers; VKBLAS_ERR_INIT without an
+ * sm_100 device. */
+typedef enum {
+    VKBLAS_PEAK_FFMA = 0,       /* fp32 fmaf, 2048 threads per SM                    */
+    VKBLAS_PEAK_TF32 = 1,       /* tcgen05.mma kind::tf32, cta_group::1, 128x256x8   */
+    VKBLAS_PEAK_TF32_PAIR = 2,  /* tcgen05.mma kind::tf32, cta_group::2, 256x256x8   */
+    VKBLAS_PEAK_F16 = 3,        /* tcgen05.mma kind::f16,  cta_group::1, 128x256x16  */
+    VKBLAS_PEAK_F16_PAIR = 4    /* tcgen05.mma kind::f16,  cta_group::2, 256x256x16  */
+} vkblas_b200_peak_t;
+vkblas_status_t vkblas_b200_peak_launch(int which, uint32_t iters, void* stream, int* status,
+                                        double* flops);
+
 /* Multi-GPU shard planner (pure host logic).  Splits `units` work units
  * (batch entries, or column blocks of `block` columns) into `world` contiguous
  * ranges as evenly as possible; returns this rank's [begin, begin+count).

@@ -5,7 +5,9 @@
 #include <stddef.h>
 
 #define FAKE_HANDLE ((void*)0x5EA1)
-int fake_last_call = 0;          /* 1 sdot, 2 sgemm, 3 dgemm, 4 setstream, 5 rocblas_gemm_ex */
+int fake_last_call = 0;          /* 1 sdot, 2 sgemm, 3 dgemm, 4 setstream, 5 rocblas_gemm_ex,
+                                    6 rocblas_gemm_strided_batched_ex */
+long long fake_last_strides[4];  /* strideA, strideB, strideC, strideD of the last call 6 */
 
 int hipblasCreate(void** h) { *h = FAKE_HANDLE; return 0; }
 int hipblasDestroy(void* h) { return h == FAKE_HANDLE ? 0 : 3; }
@@ -46,4 +48,19 @@ int rocblas_gemm_ex(void* h, int ta, int tb, int m, int n, int k, const void* al
     fake_last_call = 5;
     return h == FAKE_HANDLE ? 0 : 1;
 }
+int rocblas_gemm_strided_batched_ex(void* h, int ta, int tb, int m, int n, int k, const void* al,
+                                    const void* a, int at, int lda, long long sa, const void* b,
+                                    int bt, int ldb, long long sb, const void* be, const void* c,
+                                    int ct, int ldc, long long sc, void* d, int dt, int ldd,
+                                    long long sd, int batch, int comp, int algo, int32_t sol,
+                                    uint32_t flags) {
+    (void)ta; (void)tb; (void)m; (void)n; (void)k; (void)al; (void)a; (void)at; (void)lda;
+    (void)b; (void)bt; (void)ldb; (void)be; (void)c; (void)ct; (void)ldc; (void)d; (void)dt;
+    (void)ldd; (void)batch; (void)comp; (void)algo; (void)sol; (void)flags;
+    fake_last_call = 6;
+    fake_last_strides[0] = sa; fake_last_strides[1] = sb;
+    fake_last_strides[2] = sc; fake_last_strides[3] = sd;
+    return h == FAKE_HANDLE ? 0 : 1;
+}
+long long fake_get_last_stride(int i) { return fake_last_strides[i]; }
 int fake_get_last_call(void) { return fake_last_call; }

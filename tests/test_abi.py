@@ -131,6 +131,34 @@ def test_rocblas_rules_without_device_work():
             vk.rocblas_status_not_implemented
 
 
+def _roc_sb(h, m=4, n=4, k=4, c=16, d=16, ldc=4, ldd=4, sc=16, sd=16, batch=2, dt=150, comp=151):
+    """rocblas_gemm_strided_batched_ex with dummy pointers (nothing is dereferenced
+    on a path that validates or forwards)."""
+    al, be = hb.fptr(1.0), hb.fptr(0.0)
+    return vk.lib.rocblas_gemm_strided_batched_ex(
+        h.h, 111, 111, m, n, k, al, 0x1000, dt, 4, 16, 0x2000, dt, 4, 16, be, c, dt, ldc, sc, d, dt,
+        ldd, sd, batch, comp, 0, 0, 0)
+
+
+def test_rocblas_strided_batched_rules_without_device_work():
+    """rocblas_gemm_strided_batched_ex (src/vkblas_hipblas.c:893-955): sizes are
+    checked first; only in-place calls with fp32 compute reach the engine, and
+    everything else is forwarded (not_implemented without a real rocBLAS)."""
+    with hb.RocHandle() as h:
+        assert _roc_sb(h, m=0) == vk.rocblas_status_invalid_value        # :902
+        assert _roc_sb(h, k=-1) == vk.rocblas_status_invalid_value
+        assert _roc_sb(h, batch=0) == vk.rocblas_status_invalid_value
+        nimpl = vk.rocblas_status_not_implemented
+        assert _roc_sb(h, d=32) == nimpl                                   # c != d
+        assert _roc_sb(h, ldd=8) == nimpl                                  # ldc != ldd
+        assert _roc_sb(h, comp=150) == nimpl                               # compute f16
+        assert _roc_sb(h, dt=170) == nimpl                                 # unknown dtype
+        assert _roc_sb(h, sd=32) == nimpl                                  # strideC != strideD
+    assert vk.lib.rocblas_gemm_strided_batched_ex(
+        None, 111, 111, 4, 4, 4, None, 0, 150, 4, 16, 0, 150, 4, 16, None, 16, 150, 4, 16, 16, 150,
+        4, 16, 2, 151, 0, 0, 0) == vk.rocblas_status_invalid_value        # no handle
+
+
 def test_engine_validation_and_no_device():
     p = 0x10000
     assert vk.gemm(vk.DT_F32, 0, 0, 0, 4, 4, 1.0, p, 4, p, 4, 0.0, p, 4) == vk.VKBLAS_ERR_PARAM
@@ -193,6 +221,16 @@ def test_forwarding_uses_the_real_handle(tmp_path):
             st = vk.lib.rocblas_gemm_ex(h.h, 111, 111, 4, 4, 4, a1, 0, 150, 4, 0, 150, 4, b0, 16,
                                         150, 4, 32, 150, 4, 151, 0, 0, 0)
             assert st == 0 and fake.fake_get_last_call() == 5
+            # strided-batched: strideC != strideD is not in place -> forwarded with
+            # the caller's strides; an in-place call the engine cannot run (no
+            # GPU here) is forwarded too (src/vkblas_hipblas.c:951-954)
+            fake.fake_get_last_stride.restype = C.c_longlong
+            for sd, want in ((32, 32), (16, 16)):
+                st = vk.lib.rocblas_gemm_strided_batched_ex(
+                    h.h, 111, 111, 4, 4, 4, a1, 0x1000, 150, 4, 16, 0x2000, 150, 4, 16, b0, 0x3000,
+                    150, 4, 16, 0x3000, 150, 4, sd, 2, 151, 0, 0, 0)
+                assert st == 0 and fake.fake_get_last_call() == 6, (sd, st)
+                assert fake.fake_get_last_stride(3) == want
         print("OK")
     """)
     env = dict(os.environ, VKBLAS_REAL_HIPBLAS=str(so), VKBLAS_REAL_ROCBLAS=str(so))

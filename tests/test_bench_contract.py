@@ -31,26 +31,38 @@ def test_roofline_object_for_each_kernel_configuration():
     """The GPU arm's `roofline` object (built after the timed region, so a
     mistake there would cost the whole bench line) for the tile
     configurations the headline can run on: 256x256 pair tiles with a split
-    last wave, 256x128 pair tiles (whose ncu traffic is committed), and the
-    exact FFMA kernel."""
+    last wave, 256x128 pair tiles, and the exact FFMA kernel; with the
+    ceilings measured in the run and, when that measurement failed, with the
+    peak derived from the bf16 burst."""
     sys.path.insert(0, ROOT)
     import bench
-    peaks = {"hbm_gbs": 6552.0, "bf16_tflops": 1664.6, "sm_max_mhz": 1965.0}
+    peaks = {"hbm_gbs": 6548.2, "bf16_tflops": 1679.7, "sm_max_mhz": 1965.0}
+    ceil = {"ffma_fp32": {"tflops": 71.7}, "tcgen05_tf32": {"tflops": 1112.6},
+            "tcgen05_tf32_pair": {"tflops": 1111.0}, "tcgen05_f16": {"tflops": 2213.8},
+            "tcgen05_f16_pair": {"tflops": 2059.7}}
     flop = 2.0 * 4096 ** 3
     gemm_ms, step_ms = 0.465, 0.548
-    wide = bench._roofline("tc", 256, True, 2, gemm_ms, step_ms, peaks, "measured")
+    wide = bench._roofline("tc", 256, True, 2, gemm_ms, step_ms, peaks, "measured", ceil)
     assert wide["kernel"] == ("3xTF32 tcgen05 SGEMM (umma_gemm_kernel, 256x256 tiles on CTA "
                               "pairs; last wave split 2 ways, then split_reduce_kernel)")
     assert abs(wide["achieved"] - flop / gemm_ms / 1e9) < 0.01
-    assert abs(wide["peak"] - 1664.6 / 6) < 0.01
+    assert abs(wide["peak"] - 1111.0 / 3) < 0.01 and "tcgen05_tf32_pair" in wide["peak_source"]
     assert abs(wide["frac"] - wide["achieved"] / wide["peak"]) < 1e-3
     assert abs(wide["step_achieved"] - flop / step_ms / 1e9) < 0.01
-    assert wide["traffic"] is None and wide["bound"] == "tensor" and wide["unit"] == "TFLOP/s"
+    assert wide["traffic"] == 695.2e6 and wide["bound"] == "tensor" and wide["unit"] == "TFLOP/s"
+    assert abs(wide["cublas_derived"]["peak"] - 1679.7 / 6) < 0.01
     assert wide["nominal"]["peak"] == round(1100 / 3, 1) and 0 < wide["nominal"]["frac"] < 1
-    narrow = bench._roofline("tc", 128, True, 1, 0.577, 0.658, peaks, "measured")
+    assert wide["algorithmic_bytes"] == 5 * 4096 * 4096 * 4
+    fallback = bench._roofline("tc", 256, True, 2, gemm_ms, step_ms, peaks, "measured", None)
+    assert abs(fallback["peak"] - 1679.7 / 6) < 0.01 and "bf16 burst" in fallback["peak_source"]
+    narrow = bench._roofline("tc", 128, True, 1, 0.577, 0.658, peaks, "measured", ceil)
     assert narrow["kernel"].endswith("256x128 tiles on CTA pairs)")
     assert narrow["traffic"] == 923.4e6
-    ffma = bench._roofline("simt", 0, False, 1, 3.7, 3.7, peaks, "measured")
+    single = bench._roofline("tc", 128, False, 1, 0.6, 0.7, peaks, "measured", ceil)
+    assert single["traffic"] is None and abs(single["peak"] - 1112.6 / 3) < 0.01
+    ffma = bench._roofline("simt", 0, False, 1, 3.7, 3.7, peaks, "measured", ceil)
     assert ffma["kernel"] == "FFMA SIMT SGEMM" and "nominal" not in ffma
-    assert abs(ffma["peak"] - 148 * 128 * 2 * 1.965e-3) < 0.01
+    assert ffma["peak"] == 71.7
+    ffma_nom = bench._roofline("simt", 0, False, 1, 3.7, 3.7, peaks, "measured", None)
+    assert abs(ffma_nom["peak"] - 148 * 128 * 2 * 1.965e-3) < 0.01
     json.dumps(wide)

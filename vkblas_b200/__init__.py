@@ -87,6 +87,8 @@ def _load() -> C.CDLL:
     lib.vkblas_shard_range.restype = i32
     lib.vkblas_b200_tc_plan.argtypes = [i32, i32, i32, u32, u32, u32, u32, i32, i32, vp]
     lib.vkblas_b200_tc_plan.restype = i32
+    lib.vkblas_b200_peak_launch.argtypes = [i32, u32, vp, vp, C.POINTER(C.c_double)]
+    lib.vkblas_b200_peak_launch.restype = i32
     return lib
 
 

@@ -860,7 +860,10 @@ SHIM_EXPORT rocblas_status rocblas_gemm_ex(rocblas_handle handle, rocblas_operat
                   solution_index, flags);
 }
 
-// src/vkblas_hipblas.c:893-955
+// src/vkblas_hipblas.c:893-955.  In place means the same D as C: c == d,
+// ldc == ldd and, with more than one batch entry, strideC == strideD.  The
+// reference checks only the first two and writes D at strideC; a call whose
+// strides differ is forwarded here instead.
 SHIM_EXPORT rocblas_status rocblas_gemm_strided_batched_ex(
     rocblas_handle handle, rocblas_operation transA, rocblas_operation transB, rocblas_int m,
     rocblas_int n, rocblas_int k, const void* alpha, const void* a, rocblas_datatype a_type,
@@ -873,9 +876,10 @@ SHIM_EXPORT rocblas_status rocblas_gemm_strided_batched_ex(
     if (!h) return rocblas_status_invalid_value;
     if (m <= 0 || n <= 0 || k <= 0 || batch_count <= 0) return rocblas_status_invalid_value;
     int dt = roc_dtype(a_type, b_type, c_type, d_type);
-    if (c == d && ldc == ldd && compute_type == rocblas_datatype_f32_r && dt >= 0) {
+    const bool same_d = c == d && ldc == ldd && (batch_count == 1 || strideC == strideD);
+    if (same_d && compute_type == rocblas_datatype_f32_r && dt >= 0) {
         Run r = run_gemm(h, (vkblas_dtype_t)dt, roc_to_hip_op(transA), roc_to_hip_op(transB), m, n,
-                         k, alpha, a, lda, strideA, b, ldb, strideB, beta, d, ldd, strideC,
+                         k, alpha, a, lda, strideA, b, ldb, strideB, beta, d, ldd, strideD,
                          batch_count, false);
         if (r == Run::Done) return rocblas_status_success;
         if (r == Run::Invalid) return rocblas_status_invalid_value;
