@@ -275,11 +275,35 @@ def secondary_results(vk, hb, torch, peaks, ceil=None):
     return out
 
 
-def sharded_config5(vk, torch, dist, rank, world, stream):
-    """BASELINE config 5 across the ranks: 256 x 2048^3 fp16 NN strided-batched,
-    sharded by batch (weak in the number of GEMMs per rank), timed without and
-    with the all-gather that replicates C (2 GiB) on every rank; max over ranks."""
+def _max_over_ranks(torch, dist, ms):
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
+    """The sharded BASELINE configs across the ranks (device time, max over
+    ranks), each without the gather that replicates C and with it:
+
+    * config 5, 256 x 2048^3 fp16 NN strided-batched, sharded by batch: the
+      gather as one all-gather after the GEMM, and pipelined (chunks = 4:
+      point-to-point gathers of quarter shards, each on a side stream as soon
+      as its GEMM quarter is done);
+    * config 3 at 16384^3 (fp16, hipBLAS T/N) sharded by column blocks of C,
+      the gather pipelined the same way.
+
+    For each: the GEMM time, the time the gather adds, and which of the two
+    bounds the step."""
     from vkblas_b200 import shard
+    out = {}
+
+    def timed(run, reps):
+        run()
+        torch.cuda.synchronize()
+        dist.barrier()
+        return _max_over_ranks(torch, dist, _time_loop(lambda i: run(), reps, stream))
+
+    # config 5
     b, n = 256, 2048
     b0, cnt = shard.batch_shard(b, rank, world)
     g = torch.Generator(device="cuda").manual_seed(500 + rank)
@@ -288,29 +312,54 @@ def sharded_config5(vk, torch, dist, rank, world, stream):
     C_full = torch.empty(b * n * n, device="cuda", dtype=torch.float16)
     C_local = C_full[b0 * n * n: (b0 + cnt) * n * n]
 
-    def run(gather):
+    def run5(gather, chunks):
         shard.sharded_batched_gemm(vk.DT_F16, 0, 0, n, n, n, 1.0, A, n, n * n, B, n, n * n, 0.0,
                                    C_local, n, n * n, b, rank=rank, world=world,
-                                   C_full=C_full if gather else None)
-    out = {}
-    for gather in (False, True):
-        run(gather)
-        torch.cuda.synchronize()
-        dist.barrier()
-        ms = _time_loop(lambda i: run(gather), 3, stream)
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        key = "with_allgather" if gather else "gemm_only"
-        out[key] = {"ms": round(ms, 3), "tflops": round(b * 2.0 * n ** 3 / ms / 1e9, 2)}
-    out["allgather_ms"] = round(out["with_allgather"]["ms"] - out["gemm_only"]["ms"], 3)
-    out["allgather_bytes"] = b * n * n * 2
+                                   C_full=C_full if gather else None, status_group=status_group,
+                                   chunks=chunks)
+    flop5 = b * 2.0 * n ** 3
+    r5 = {}
+    for key, gather, chunks in (("gemm_only", False, 1), ("with_allgather", True, 1),
+                                ("with_pipelined_gather", True, 4)):
+        ms = timed(lambda: run5(gather, chunks), 5)
+        r5[key] = {"ms": round(ms, 3), "tflops": round(flop5 / ms / 1e9, 2)}
+    r5["gather_ms"] = round(r5["with_allgather"]["ms"] - r5["gemm_only"]["ms"], 3)
+    r5["pipelined_extra_ms"] = round(r5["with_pipelined_gather"]["ms"] - r5["gemm_only"]["ms"], 3)
+    r5["gather_bytes_per_rank"] = (b - cnt) * n * n * 2
+    r5["bound"] = "gather" if r5["gather_ms"] > r5["gemm_only"]["ms"] else "gemm"
+    out["hgemm_batched_256x2048_sharded"] = r5
     del A, B, C_full, C_local
+    torch.cuda.empty_cache()
+
+    # config 3 at 16384^3, column blocks of C (hipBLAS T/N: A is K x M, lda = K)
+    m = k = nn = 16384
+    c0, cc = shard.column_shard(nn, rank, world, 256)
+    g = torch.Generator(device="cuda").manual_seed(600 + rank)
+    A = (torch.randn(k * m, device="cuda", generator=g) * 0.02).half()
+    Bc = (torch.randn(max(cc, 1) * k, device="cuda", generator=g) * 0.02).half()
+    C_full = torch.empty(m * nn, device="cuda", dtype=torch.float16)
+    C_cols = C_full[c0 * m: (c0 + cc) * m]
+
+    def run3(gather, chunks):
+        shard.sharded_column_gemm_hip(vk.DT_F16, 1, 0, m, nn, k, 1.0, A, k, Bc, k, 0.0, C_cols, m,
+                                      rank=rank, world=world, C_full=C_full if gather else None,
+                                      status_group=status_group, chunks=chunks)
+    flop3 = 2.0 * m * nn * k
+    r3 = {}
+    for key, gather, chunks in (("gemm_only", False, 1), ("with_pipelined_gather", True, 4)):
+        ms = timed(lambda: run3(gather, chunks), 3)
+        r3[key] = {"ms": round(ms, 3), "tflops": round(flop3 / ms / 1e9, 2)}
+    r3["pipelined_extra_ms"] = round(r3["with_pipelined_gather"]["ms"] - r3["gemm_only"]["ms"], 3)
+    r3["gather_bytes_per_rank"] = (nn - cc) * m * 2
+    out["hgemm_tn_16384_column_sharded"] = r3
+    del A, Bc, C_full, C_cols
+    torch.cuda.empty_cache()
     return out
 
 
 # ------------------------------------------------------- single-case runner
-CASES = ["sgemm", "sgemm-simt", "hgemm", "gemv", "gemv32", "batched", "dgemm", "zgemm", "peaks"]
+CASES = ["sgemm", "sgemm-simt", "hgemm", "gemv", "gemv32", "batched", "dgemm", "zgemm", "peaks",
+         "cpu"]
 
 
 def run_peaks(vk, torch, stream, reps=3):
@@ -344,6 +393,101 @@ def run_peaks(vk, torch, stream, reps=3):
     return out
 
 
+def run_cpu_baselines(budget_s: float = 6.0) -> dict:
+    """The reference's own CPU GEMMs timed on this host (oracle/_ref, compiled
+    from the reference's test/test_gemm.c and test/test_h.c; the oracle's port
+    of ref_gemm when that build is absent), for every BASELINE config:
+
+    * ref_gemm (test/test_gemm.c:32-58), config 2 (4096^3 NN), row-sampled as
+      the reference itself samples rows (test/test_gemm.c:36-43), on 1 thread
+      and on all threads;
+    * ref_gemm, config 1 (1024^3, alpha 1.5, beta 0.5) in full, all four ops,
+      all threads;
+    * cpu_ref (test/test_h.c:63-79), config 3 (fp16, hipBLAS T/N, M=N=K in
+      {4096, 8192, 16384}) on a sample of C's columns, all threads;
+    * cpu_ref, config 4 (decode, M in {1, 4, 16} x 4096 -> 14336) in full, all
+      threads (split over C's columns, so M = 1 uses them too).
+
+    TFLOP/s = 2 x the multiply-adds of what ran / wall time.  ``budget_s``
+    bounds each sampled measurement."""
+    import platform
+    import numpy as np
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    ref = orc.ref
+    out = {"host": {"nproc": threads, "cpu": platform.processor() or platform.machine()},
+           "kind": "reference" if ref is not None else "port"}
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    out["host"]["cpu"] = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    rows_fn = ref.vkref_ref_gemm_rows_mt if ref is not None else orc.lib.orc_sgemm_colmajor_rows_mt
+    rng = np.random.default_rng(0)
+
+    def sgemm_rows(n, ta, tb, alpha, beta, rows, nthr, A, B, C):
+        t0 = time.perf_counter()
+        rows_fn(ta, tb, n, n, n, alpha, A, n, B, n, beta, C, n, 0, rows, nthr)
+        return time.perf_counter() - t0
+
+    n = 4096
+    A = rng.standard_normal(n * n, dtype=np.float32)
+    B = rng.standard_normal(n * n, dtype=np.float32)
+    C = np.zeros(n * n, np.float32)
+    for nthr in (1, threads):
+        per_row = sgemm_rows(n, 0, 0, 1.0, 0.0, nthr, nthr, A, B, C) / nthr   # wall per row
+        rows = int(min(n, max(nthr, budget_s / max(per_row, 1e-6))))
+        rows = max(nthr, rows // nthr * nthr)
+        dt = sgemm_rows(n, 0, 0, 1.0, 0.0, rows, nthr, A, B, C)
+        out[f"cfg2_sgemm_4096_nn_{nthr}t"] = {
+            "tflops": 2.0 * rows * n * n / dt / 1e12, "threads": nthr,
+            "sample": f"{rows} of 4096 rows, {dt:.2f} s"}
+    n = 1024
+    A1 = rng.uniform(-1, 1, n * n).astype(np.float32)
+    B1 = rng.uniform(-1, 1, n * n).astype(np.float32)
+    for ta, tb in ((0, 0), (0, 1), (1, 0), (1, 1)):
+        C1 = rng.uniform(-1, 1, n * n).astype(np.float32)
+        dt = sgemm_rows(n, ta, tb, 1.5, 0.5, n, threads, A1, B1, C1)
+        out[f"cfg1_sgemm_1024_{'NT'[ta]}{'NT'[tb]}"] = {
+            "tflops": 2.0 * n ** 3 / dt / 1e12, "threads": threads, "sample": f"full, {dt:.2f} s"}
+    if ref is None:
+        return out
+    half = ref.vkref_cpu_ref_half_cols_mt
+    for n in (4096, 8192, 16384):
+        # hipBLAS T/N, column-major C (n x n) = A^T B: the engine call (N, T) with
+        # M = n rows of B's columns and N = n; a sample of C's columns
+        Ah = orc.f2h((rng.standard_normal(n * n) * 0.02).astype(np.float32))
+        Bh = orc.f2h((rng.standard_normal(n * n) * 0.02).astype(np.float32))
+        Ch = np.zeros(n * n, np.uint16)
+        t0 = time.perf_counter()
+        half(0, 0, 1, n, n, n, Bh, n, Ah, n, 1.0, 0.0, Ch, n, 0, threads, threads)
+        per_col = (time.perf_counter() - t0) / threads     # wall time per column, all threads
+        cols = int(min(n, max(threads, budget_s / max(per_col, 1e-6))))
+        cols = max(threads, cols // threads * threads)
+        t0 = time.perf_counter()
+        half(0, 0, 1, n, n, n, Bh, n, Ah, n, 1.0, 0.0, Ch, n, 0, cols, threads)
+        dt = time.perf_counter() - t0
+        out[f"cfg3_hgemm_tn_{n}"] = {"tflops": 2.0 * n * n * cols / dt / 1e12, "threads": threads,
+                                      "sample": f"{cols} of {n} columns of C, {dt:.2f} s"}
+        del Ah, Bh, Ch
+    K, O = 4096, 14336
+    W = orc.f2h((rng.standard_normal(O * K) * 0.02).astype(np.float32))
+    for m in (1, 4, 16):
+        X = orc.f2h(rng.standard_normal(m * K).astype(np.float32))
+        Cd = np.zeros(m * O, np.uint16)
+        t0 = time.perf_counter()
+        half(0, 0, 1, m, O, K, X, K, W, K, 1.0, 0.0, Cd, O, 0, O, threads)
+        dt = time.perf_counter() - t0
+        nbytes = 2.0 * (O * K + m * K + m * O)
+        out[f"cfg4_decode_m{m}"] = {"gbs": nbytes / dt / 1e9, "us": dt * 1e6,
+                                    "tflops": 2.0 * m * O * K / dt / 1e12, "threads": threads,
+                                    "sample": f"full, {dt:.3f} s"}
+    return out
+
+
 def run_case(a) -> int:
     """One GEMM case of the BASELINE configs, `--iters` times on torch's current
     stream after one untimed call (for timing and ncu captures):
@@ -356,9 +500,14 @@ def run_case(a) -> int:
         python bench.py --case dgemm|zgemm [--n 2048]              # fp64 / complex128 N/N
         python bench.py --case batched                             # 256 x 2048^3 fp16 N/N
         python bench.py --case peaks                               # tcgen05 / FFMA ceilings
+        python bench.py --case cpu                                 # the reference's CPU GEMMs
 
     Inputs are device-resident and seeded; the mean time per call (CUDA
-    events) is printed.  --path simt|tc|gemv forces a kernel family."""
+    events) is printed.  --path simt|tc|gemv forces a kernel family; --graph
+    replays the calls from a CUDA graph (kernel time without host launch gaps)."""
+    if a.case == "cpu":
+        print(json.dumps(run_cpu_baselines()))
+        return 0
     import torch
     import vkblas_b200 as vk
     from vkblas_b200 import hipblas as hb
@@ -372,7 +521,9 @@ def run_case(a) -> int:
         print(json.dumps(res))
         return 0
     torch.cuda.init()
-    s = torch.cuda.current_stream()
+    # CUDA graphs cannot be captured on the legacy default stream
+    s = torch.cuda.Stream() if a.graph else torch.cuda.current_stream()
+    torch.cuda.set_stream(s)
     g = torch.Generator(device="cuda").manual_seed(0)
     al, be = hb.fptr(1.0), hb.fptr(0.0)
     h = hb.Handle()
@@ -469,12 +620,29 @@ def run_case(a) -> int:
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(a.iters):
-        call()
-    e1.record(s)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / max(1, a.iters)
+    if a.graph:
+        # the calls captured once and replayed: no host launch gaps
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for _ in range(a.iters):
+                call()
+        graph.replay()
+        torch.cuda.synchronize()
+        reps = 5
+        e0.record(s)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * max(1, a.iters))
+        del graph
+    else:
+        e0.record(s)
+        for _ in range(a.iters):
+            call()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / max(1, a.iters)
     st = vk.device_status(True)
     line = f"{a.case}: {ms * 1e3:.2f} us/call, {flop / ms / 1e9:.2f} TFLOP/s"
     if nbytes:
@@ -570,6 +738,8 @@ def main() -> int:
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc", "gemv"],
                     help="--case: force a kernel family (vkblas_b200_set_path)")
+    ap.add_argument("--graph", action="store_true",
+                    help="--case: capture the --iters calls in a CUDA graph and time 5 replays")
     args = ap.parse_args()
     if args.case:
         return run_case(args)
@@ -608,6 +778,9 @@ def main() -> int:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        # host-side status exchange of the sharded GEMMs (shard.py): a rank's
+        # failure reaches the others before any data collective
+        status_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
     import vkblas_b200 as vk
     from vkblas_b200 import hipblas as hb
     peaks, peaks_kind = _peaks()
@@ -766,8 +939,8 @@ def main() -> int:
             result["secondary"] = {"error": repr(exc)}
     if world > 1 and not args.no_secondary:
         # every rank takes the same collective steps; an error ends the run
-        result["secondary"] = {"hgemm_batched_256x2048_sharded": sharded_config5(
-            vk, torch, dist, rank, world, stream)}
+        result["secondary"] = sharded_secondary(vk, torch, dist, rank, world, stream,
+                                                status_group)
         torch.cuda.empty_cache()
     h.close()
     if world > 1:

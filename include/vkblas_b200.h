@@ -113,6 +113,16 @@ int vkblas_b200_device_status(int clear);
  * every role unwinds; the context stays usable.  For tests only. */
 void vkblas_b200_set_test_stall(int on);
 
+/* Test hook for scratch-memory failure (thread-local, off by default): with
+ * count > 0 the next `count` scratch requests made from this thread fail as a
+ * failed cudaMalloc would, with count < 0 every request fails until the hook
+ * is set to 0.  A call that then lacks its scratch runs without it where it
+ * can (a GEMV or tensor-core GEMM without its K split; an fp32 GEMM on the
+ * exact SIMT kernel instead of 3xTF32 when the path is automatic) or returns
+ * VKBLAS_ERR_FALLBACK (path forced to VKBLAS_PATH_TC; the hipBLAS shim then
+ * forwards the call).  For tests only. */
+void vkblas_b200_set_test_alloc_fail(int count);
+
 /* Number of kernels this library launched from the calling process (all
  * threads); used by tests and benchmarks to prove the native path ran. */
 uint64_t vkblas_b200_launch_count(void);
@@ -127,8 +137,9 @@ const char* vkblas_b200_version(void);
  * whether 256-wide 3xTF32 pair tiles may be chosen (the launch path allows
  * them when its kernel's register split fits and VKBLAS_TF32_WIDE is not 0).
  * The plan assumes the K-split is on (VKBLAS_TC_SPLIT) and its scratch can be
- * had.  Returns VKBLAS_ERR_PARAM for a zero size, num_sms < 1, an unknown dtype
- * or a null `out`.  No counterpart in the reference. */
+ * had.  Returns VKBLAS_ERR_PARAM for a zero size, num_sms < 1, an unknown dtype,
+ * a null `out`, or 2^31 tiles or more (a call the tensor-core path rejects).
+ * No counterpart in the reference. */
 typedef struct {
     uint32_t tile_m;             /* rows of a tile: 128, or 256 on CTA pairs */
     uint32_t tile_n;             /* columns of a tile */

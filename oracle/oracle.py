@@ -74,6 +74,8 @@ def _load_ref():
     lib.vkref_ref_gemm_rows_mt.argtypes = [_i, _i, _i, _i, _i, _f, _f32p, _i, _f32p, _i, _f, _f32p,
                                            _i, _i, _i, _i]
     lib.vkref_cpu_ref_half.argtypes = [_i, _i, _i, _i, _i, _i, _u16p, _i, _u16p, _i, _f, _f, _u16p, _i]
+    lib.vkref_cpu_ref_half_cols_mt.argtypes = [_i, _i, _i, _i, _i, _i, _u16p, _i, _u16p, _i, _f, _f,
+                                               _u16p, _i, _i, _i, _i]
     lib.vkref_f2h.restype = C.c_uint16
     lib.vkref_f2h.argtypes = [_f]
     lib.vkref_h2f.restype = _f

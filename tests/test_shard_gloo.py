@@ -83,6 +83,66 @@ def _worker(rank, world, port, kind):
         dist.destroy_process_group()
 
 
+def _worker_pipelined(rank, world, port):
+    """chunks > 1: the shards are cut into pieces whose gathers are point-to-point
+    sends and receives issued piece by piece (overlapped with the GEMM on a GPU);
+    uneven shards, pieces that are empty on some ranks, C_local aliased to
+    C_full or a separate buffer."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    from vkblas_b200 import shard
+    rng = np.random.default_rng(5)
+    try:
+        M, N, K = 12, 10, 8
+        for batch, chunks, aliased in ((7, 3, True), (8, 4, False), (5, 4, True), (3, 4, False)):
+            sa, sb, sc = M * K, K * N, M * N
+            A = rng.uniform(-1, 1, sa * batch).astype(np.float32)
+            B = rng.uniform(-1, 1, sb * batch).astype(np.float32)
+            C0 = rng.uniform(-1, 1, sc * batch).astype(np.float32)
+            want = C0.copy()
+            orc.gemm_rowmajor_f32seq(0, 0, M, N, K, 1.25, A, K, B, N, -0.5, want, N, batch, sa, sb, sc)
+            b0, n = shard.batch_shard(batch, rank, world)
+            full = torch.zeros(sc * batch)
+            mine = torch.from_numpy(C0[b0 * sc: (b0 + n) * sc]).clone()
+            if aliased:
+                Cl = full[b0 * sc: (b0 + n) * sc]
+                Cl.copy_(mine)
+            else:
+                Cl = mine
+            shard.sharded_batched_gemm(0, 0, 0, M, N, K, 1.25,
+                                       torch.from_numpy(A[b0 * sa: (b0 + n) * sa]).clone(), K, sa,
+                                       torch.from_numpy(B[b0 * sb: (b0 + n) * sb]).clone(), N, sb,
+                                       -0.5, Cl, N, sc, batch, rank=rank, world=world,
+                                       C_full=full, gemm_fn=_cpu_gemm, chunks=chunks,
+                                       status_group=dist.group.WORLD)
+            assert np.array_equal(full.numpy(), want), f"rank {rank} batch {batch} chunks {chunks}"
+            assert np.array_equal(Cl.numpy(), want[b0 * sc: (b0 + n) * sc])
+        m, n, k = 20, 300, 16                 # hipBLAS column-major C(m x n), blocks of 64
+        for transB in (0, 1):
+            A = rng.uniform(-1, 1, m * k).astype(np.float32)
+            B = rng.uniform(-1, 1, k * n).astype(np.float32)
+            ldb = k if transB == 0 else n
+            want = np.zeros(m * n, np.float32)
+            orc.gemm_rowmajor_f32seq(transB, 0, n, m, k, 1.0, B, ldb, A, m, 0.0, want, m)
+            c0, cnt = shard.column_shard(n, rank, world, block=64)
+            full = torch.zeros(m * n)
+            Bc = torch.from_numpy(B[c0 * ldb: (c0 + cnt) * ldb] if transB == 0 else B).clone()
+            shard.sharded_column_gemm_hip(0, 0, transB, m, n, k, 1.0, torch.from_numpy(A), m, Bc,
+                                          ldb, 0.0, full[c0 * m: (c0 + cnt) * m], m, rank=rank,
+                                          world=world, C_full=full, block=64, gemm_fn=_cpu_gemm,
+                                          chunks=3)
+            assert np.array_equal(full.numpy(), want), f"rank {rank} column pieces"
+    finally:
+        dist.destroy_process_group()
+
+
 @pytest.mark.parametrize("kind", ["batch", "columns"])
 def test_sharded_gemm_two_gloo_ranks(kind):
     mp.spawn(_worker, args=(2, _free_port(), kind), nprocs=2, join=True)
+
+
+def test_pipelined_gather_two_gloo_ranks():
+    mp.spawn(_worker_pipelined, args=(2, _free_port()), nprocs=2, join=True)

@@ -33,7 +33,7 @@ def _mk(dtype, rng, n):
 
 
 def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8, split=None,
-         pair=None):
+         pair=None, tile_n=None):
     import torch
     rng = np.random.default_rng(M * 7 + N * 3 + K + op_a * 2 + op_b + dtype * 11 + batch)
     lda = (M if op_a else K)
@@ -75,6 +75,8 @@ def _run(dtype, op_a, op_b, M, N, K, alpha, beta, batch=1, bcast=None, ldc_pad=8
         assert (vk.last_split() > 1) == split, f"K-split count {vk.last_split()}"
     if pair is not None:
         assert vk.last_pair() == pair, f"CTA pair mode {vk.last_pair()}"
+    if tile_n is not None:
+        assert vk.last_tile_n() == tile_n, f"tile N {vk.last_tile_n()}"
     check_status()
     got = host(dC) if dtype == vk.DT_F32 else orc.widen(dt16, host_u16(dC))
     want = orc.gemm_rowmajor_f64(op_a, op_b, M, N, K, alpha, np.ascontiguousarray(Af), lda,
@@ -237,6 +239,54 @@ def test_tc_pair_wave_tail_split(dtype, cuda):
     """75 pair tiles (one per batch entry) on 74 SM pairs: whole waves run
     unsplit, only the last pair tile is split along K."""
     _run(dtype, 0, 0, 256, 40, 4096, 1.0, 0.0, batch=75, split=True, pair=True)
+
+
+@pytest.mark.parametrize("ops", [(0, 0), (1, 1)], ids=["NN", "TT"])
+@pytest.mark.parametrize("split", [False, True], ids=["whole", "split"])
+def test_tf32_wide_pair_tiles(ops, split, cuda):
+    """fp32 GEMMs with M >= 256 and N >= 256 run on the 256 x 256 3xTF32 pair
+    tiles (the headline's kernel), whole and with a split last wave."""
+    M, N, K = (256, 256, 4096) if split else (512, 768, 256)
+    _run(vk.DT_F32, ops[0], ops[1], M, N, K, 1.0, 0.5, split=split, pair=True, tile_n=256)
+
+
+_NARROW_SCRIPT = """
+import sys, numpy as np, torch
+sys.path.insert(0, {root!r}); sys.path.insert(0, {tests!r})
+import vkblas_b200 as vk
+from oracle import oracle as orc
+for (M, N, K), split in (((512, 768, 256), False), ((256, 256, 4096), True)):
+    rng = np.random.default_rng(M + N + K)
+    A = rng.uniform(-1, 1, M * K).astype(np.float32)
+    B = rng.uniform(-1, 1, K * N).astype(np.float32)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dC = torch.zeros(M * N, device="cuda")
+    vk.set_stream(torch.cuda.current_stream())
+    assert vk.gemm(vk.DT_F32, 0, 0, M, N, K, 1.0, dA.data_ptr(), K, dB.data_ptr(), N, 0.0,
+                   dC.data_ptr(), N) == vk.VKBLAS_OK
+    torch.cuda.synchronize()
+    assert vk.last_path() == vk.PATH_TC and vk.last_pair() and vk.last_tile_n() == 128, \
+        (vk.last_path(), vk.last_pair(), vk.last_tile_n())
+    assert (vk.last_split() > 1) == split, vk.last_split()
+    want = orc.gemm_rowmajor_f64(0, 0, M, N, K, 1.0, A, K, B, N, 0.0, None, N)[0]
+    err = orc.rel_frobenius(dC.cpu().numpy().reshape(M, N), want)
+    assert err <= 1e-5, err
+    assert vk.device_status(True) == 0
+print("OK")
+"""
+
+
+def test_tf32_narrow_pair_tiles_when_wide_is_off(cuda):
+    """VKBLAS_TF32_WIDE=0 keeps the 256 x 128 pair tiles for N >= 256 (read once
+    per process, so in a child process), whole and split; oracle-checked."""
+    import os
+    import subprocess
+    import sys
+    tests = os.path.dirname(os.path.abspath(__file__))
+    code = _NARROW_SCRIPT.format(root=os.path.dirname(tests), tests=tests)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, VKBLAS_TF32_WIDE="0"))
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr[-3000:]
 
 
 def test_tf32_transposed_split_beyond_grid_y_limit(cuda):

@@ -117,3 +117,13 @@ def test_rejects_bad_arguments():
                  (F32, 0, 0, 8, 8, 8, 1, 0), (7, 0, 0, 8, 8, 8, 1, SMS)):
         with pytest.raises(vk.VkblasError):
             vk.tc_plan(*args)
+
+
+def test_rejects_tile_counts_the_launch_path_rejects():
+    """2^31 tiles or more: the tensor-core launch refuses the call, so the plan
+    query reports VKBLAS_ERR_PARAM instead of a truncated tile count."""
+    for dt in (F32, F16):
+        with pytest.raises(vk.VkblasError):
+            vk.tc_plan(dt, 0, 0, 4096, 4096, 64, 1 << 24, SMS)     # 16 x 16 x 2^24 = 2^32 tiles
+    p = vk.tc_plan(F16, 0, 0, 4096, 4096, 64, (1 << 23) - 1, SMS)  # just under 2^31
+    assert p["tiles"] == 256 * ((1 << 23) - 1)

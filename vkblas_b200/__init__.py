@@ -74,6 +74,7 @@ def _load() -> C.CDLL:
     lib.vkblas_b200_last_tile_n.restype = i32
     lib.vkblas_b200_set_splitk.argtypes = [i32]
     lib.vkblas_b200_set_test_stall.argtypes = [i32]
+    lib.vkblas_b200_set_test_alloc_fail.argtypes = [i32]
     lib.vkblas_b200_device_status.argtypes = [i32]
     lib.vkblas_b200_device_status.restype = i32
     lib.vkblas_b200_launch_count.restype = C.c_uint64

@@ -105,12 +105,23 @@ DeviceState* device_state(int dev) {
     return d;
 }
 
+// Test hook (vkblas_b200_set_test_alloc_fail): while non-zero, every scratch
+// request made from this thread fails as a failed cudaMalloc would; a positive
+// count runs down by one per request.
+thread_local int tls_fail_alloc = 0;
+
 // Grow-only scratch per (device, kind, stream).  Growth frees the old buffer
 // (cudaFree waits for the device) and zero-fills the new one on the stream,
 // which is what the GEMV split-K tickets need.  Not callable during stream
-// capture: make one call of the largest shape before capturing.
+// capture: make one call of the largest shape before capturing.  Returns
+// nullptr when the memory cannot be had; every caller then runs without the
+// scratch (no split) or declines the call (the hipBLAS shim forwards it).
 void* workspace(DeviceState* ds, int kind, cudaStream_t s, size_t bytes) {
     if (bytes == 0) return nullptr;
+    if (tls_fail_alloc) {
+        if (tls_fail_alloc > 0) tls_fail_alloc--;
+        return nullptr;
+    }
     std::lock_guard<std::mutex> lk(ds->mu);
     Workspace& w = ds->ws[kind][s];
     if (w.bytes >= bytes) return w.ptr;
@@ -512,6 +523,8 @@ VKB_EXPORT void vkblas_b200_set_splitk(int splitk) {
 
 VKB_EXPORT void vkblas_b200_set_test_stall(int on) { tls.test_stall = on ? 1 : 0; }
 
+VKB_EXPORT void vkblas_b200_set_test_alloc_fail(int count) { tls_fail_alloc = count; }
+
 VKB_EXPORT void vkblas_b200_set_kernel_events(void* start, void* end) {
     tls.ev_start = start;
     tls.ev_end = end;
@@ -581,6 +594,7 @@ VKB_EXPORT vkblas_status_t vkblas_b200_tc_plan(vkblas_dtype_t dtype, vkblas_op_t
     GemmProblem p = make_problem((int)dtype, op_a, op_b, M, N, K, 1.f, nullptr, 0, nullptr, 0, 0.f,
                                  nullptr, 0, batch, 0, 0, 0);
     const UmmaPlan r = umma_plan(p, num_sms, allow_wide != 0);
+    if (r.too_many_tiles) return VKBLAS_ERR_PARAM;     // the launch path rejects such a call too
     out->tile_m = r.tile_m;
     out->tile_n = r.tile_n;
     out->transposed = r.transposed;

@@ -27,6 +27,7 @@
 //     ticket, no waiting) reduces them in segment order, applies alpha/beta
 //     and resets its ticket for the next launch.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -35,11 +36,11 @@
 namespace vkb {
 namespace {
 
-constexpr int KW = 8;                    // warps per CTA, splitting K (M <= 8)
-// With two token tiles (M > 8) a thread needs 64 registers; 4 warps per CTA
-// then keep all 896 CTAs of a 14336-row layer resident in one wave (measured
-// 27.0 us against 29.0 us with 8 warps at M = 16).
-template <bool TWO_NTILES> constexpr int kw_of() { return TWO_NTILES ? 4 : KW; }
+// Warps per CTA (they split the CTA's K range).  A thread needs 61-64
+// registers, so an SM holds 4 CTAs of 8 warps or 8 CTAs of 4 warps.  4-warp
+// CTAs keep all 896 CTAs of a 14336-row layer resident in one wave (measured at
+// M = 16: 27.0 us against 29.0 us with 8 warps); 8-warp CTAs give a short
+// layer (few row blocks) more warps per row block.  See gemv_warps().
 constexpr int ROWS_PER_CTA = 16;         // weight rows per CTA (one m16 MMA tile)
 constexpr int KCHUNK = 64;
 
@@ -104,9 +105,8 @@ __device__ __forceinline__ void mma_32k(float (&d)[4], const uint4& w_lo, const 
     Mma<T>::run(d, a1, x.z, x.w);
 }
 
-template <typename T, bool TWO_NTILES>
-__global__ void __launch_bounds__(kw_of<TWO_NTILES>() * 32) gemv_kernel(GemvArgs a) {
-    constexpr int KW = kw_of<TWO_NTILES>();
+template <typename T, bool TWO_NTILES, int KW>
+__global__ void __launch_bounds__(KW * 32) gemv_kernel(GemvArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t nbase = blockIdx.x * ROWS_PER_CTA;
@@ -265,6 +265,38 @@ uint32_t gemv_kspan(uint32_t K, int splitk) {
     return (span + KCHUNK - 1) / KCHUNK * KCHUNK;
 }
 
+// Warps per CTA: 4 when M > 8 (two token tiles); for M <= 8, 8 unless the
+// row-block CTAs of all segments would not fit in one wave of 4 such CTAs per
+// SM, and then 4 (8 CTAs per SM).  VKBLAS_GEMV_WARPS=4|8 fixes it for M <= 8.
+int gemv_warps(const GemmProblem& p, int splitk, int num_sms) {
+    if (p.M > 8) return 4;
+    static const int forced = [] {
+        const char* e = getenv("VKBLAS_GEMV_WARPS");
+        const int v = e ? atoi(e) : 0;
+        return (v == 4 || v == 8) ? v : 0;
+    }();
+    if (forced) return forced;
+    const uint64_t ctas = (uint64_t)((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA) * (uint64_t)splitk;
+    return ctas > 4ull * (uint64_t)num_sms ? 4 : 8;
+}
+
+int device_sms() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    return sms;
+}
+
+template <typename T>
+void launch_typed(dim3 grid, bool two, int kw, const GemvArgs& a, cudaStream_t s) {
+    if (two) gemv_kernel<T, true, 4><<<grid, 4 * 32, 0, s>>>(a);
+    else if (kw == 4) gemv_kernel<T, false, 4><<<grid, 4 * 32, 0, s>>>(a);
+    else gemv_kernel<T, false, 8><<<grid, 8 * 32, 0, s>>>(a);
+}
+
 // One launch over segments [0, segs) with the given partial/ticket areas
 // (both unused when a single segment results).
 cudaError_t launch_segments(const GemmProblem& p, int splitk, float* partial, unsigned* tickets,
@@ -282,16 +314,10 @@ cudaError_t launch_segments(const GemmProblem& p, int splitk, float* partial, un
     a.tickets = segs > 1 ? tickets : nullptr;
     dim3 grid((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA, segs);
     const bool two = p.M > 8;
-    constexpr int B1 = kw_of<false>() * 32, B2 = kw_of<true>() * 32;
-    if (p.dtype == DT_F16) {
-        if (two) gemv_kernel<__half, true><<<grid, B2, 0, s>>>(a);
-        else gemv_kernel<__half, false><<<grid, B1, 0, s>>>(a);
-    } else if (p.dtype == DT_BF16) {
-        if (two) gemv_kernel<__nv_bfloat16, true><<<grid, B2, 0, s>>>(a);
-        else gemv_kernel<__nv_bfloat16, false><<<grid, B1, 0, s>>>(a);
-    } else {
-        return cudaErrorInvalidValue;
-    }
+    const int kw = gemv_warps(p, (int)segs, device_sms());
+    if (p.dtype == DT_F16) launch_typed<__half>(grid, two, kw, a, s);
+    else if (p.dtype == DT_BF16) launch_typed<__nv_bfloat16>(grid, two, kw, a, s);
+    else return cudaErrorInvalidValue;
     count_launch();
     return cudaGetLastError();
 }
@@ -313,7 +339,7 @@ int gemv_auto_splitk(const GemmProblem& p, int num_sms) {
     // 4096 rows x K = 14336 32.6 -> 24.3 us, 4096 x 4096 13.4 -> 12.1 us;
     // without the wave cap 11008 x 4096 went from 20.5 to 26.4 us.
     const bool two = p.M > 8;
-    const uint32_t kw = two ? (uint32_t)kw_of<true>() : (uint32_t)kw_of<false>();
+    const uint32_t kw = (uint32_t)gemv_warps(p, 1, num_sms);
     const uint32_t target = (24u / kw) * (uint32_t)num_sms;
     const uint32_t wave = 8u * (uint32_t)num_sms;
     const uint32_t ctas = (p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA;

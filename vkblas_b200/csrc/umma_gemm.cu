@@ -320,6 +320,12 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
         if (warp == 0) {
             // ------------------------------------------------------ TMA producer
             if (lane == 0) {
+                // A 3xTF32 GEMM is the programmatic dependent of the split
+                // pre-pass that writes its operand planes: wait for that grid
+                // to finish and its writes to be visible before the first
+                // load.  Nothing else of this kernel reads memory the pre-pass
+                // writes.  Without a prerequisite grid this returns at once.
+                asm volatile("griddepcontrol.wait;" ::: "memory");
                 uint32_t stage = 0, phase = 0;
                 uint32_t issued_mask = 0, issued_parity = 0;   // per stage: issued ever / last parity
                 bool ok = true;
@@ -693,95 +699,124 @@ __device__ __forceinline__ float rn_tf32(float x) {
     return __uint_as_float(u & 0xFFFFE000u);
 }
 
-__global__ void split_tf32_kernel(const float* __restrict__ src, uint32_t rows, uint32_t cols,
-                                  uint32_t ld, int64_t bstride, uint32_t nb, uint32_t ldo,
-                                  float* __restrict__ big, float* __restrict__ small) {
-    const uint64_t total = (uint64_t)nb * rows * (ldo / 4);
-    const bool vec_in = (ld & 3u) == 0 && (bstride & 3) == 0 &&
-                        (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
-         i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t br = i / (ldo / 4);
-        const uint32_t c0 = (uint32_t)(i - br * (ldo / 4)) * 4u;
-        const uint32_t b = (uint32_t)(br / rows), r = (uint32_t)(br - (uint64_t)b * rows);
-        const float* s = src + bstride * (int64_t)b + (size_t)r * ld;
-        float x[4], hi[4], lo[4];
-        if (vec_in && c0 + 3 < cols) {
-            const float4 q = __ldg(reinterpret_cast<const float4*>(s + c0));
-            x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
-        } else {
+// One operand's share of the pre-pass.  K-major (mn_major == 0): src[b][r][ld]
+// with rows = M (or N) and cols = K, copied row by row.  MN-major: src[b][k][ld]
+// with rows = K and cols = M (or N), written K-major (out[b][mn][ldo], K
+// contiguous) so that the tf32 MMAs always read K-major operands.  Either way
+// the output planes are [nb][MN][ldo] with ldo = K rounded up to 4 and the pad
+// columns zero.  `blocks` CTAs of 256 threads work on it, striding over their
+// work, so no grid dimension limits K or the batch count.
+struct SplitJob {
+    const float* src;
+    uint32_t rows, cols, ld;
+    int64_t bstride;
+    uint32_t nb, ldo;
+    float* big;
+    float* small;
+    uint32_t mn_major;
+    uint32_t blocks;
+};
+
+__device__ __forceinline__ void split4(const float (&x)[4], float (&hi)[4], float (&lo)[4]) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) x[j] = (c0 + j < cols) ? __ldg(s + c0 + j) : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            hi[j] = rn_tf32(x[j]);
-            const float d = x[j] - hi[j];
-            lo[j] = isfinite(hi[j]) ? rn_tf32(d) : 0.f;
-        }
-        const uint64_t o = br * ldo + c0;
-        *reinterpret_cast<float4*>(big + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<float4*>(small + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    for (int j = 0; j < 4; j++) {
+        hi[j] = rn_tf32(x[j]);
+        lo[j] = isfinite(hi[j]) ? rn_tf32(x[j] - hi[j]) : 0.f;
     }
 }
 
-// Same split for an MN-major operand (src[b][k][ld], MN contiguous), written
-// K-major (out[b][mn][ldo], K contiguous) so that the tf32 MMAs always read
-// K-major operands.  A 64x64 tile goes through shared memory; both the global
-// reads (along MN) and the writes (along K) are 128-bit when aligned.  Blocks
-// stride over batch entries (z) and over 64-wide k tiles (y), so that K beyond
-// 65535 * 64 (a weight gradient over millions of tokens) needs no larger grid.
+// K-major operand: 4 consecutive k per thread, 128-bit loads and stores.
+__device__ __forceinline__ void split_rows(const SplitJob& j, uint32_t bid) {
+    const uint32_t q = j.ldo / 4;
+    const uint64_t total = (uint64_t)j.nb * j.rows * q;
+    const bool vec_in = (j.ld & 3u) == 0 && (j.bstride & 3) == 0 &&
+                        (reinterpret_cast<uintptr_t>(j.src) & 15u) == 0;
+    for (uint64_t i = bid * 256ull + threadIdx.x; i < total; i += (uint64_t)j.blocks * 256u) {
+        const uint64_t br = i / q;
+        const uint32_t c0 = (uint32_t)(i - br * q) * 4u;
+        const uint32_t b = (uint32_t)(br / j.rows), r = (uint32_t)(br - (uint64_t)b * j.rows);
+        const float* s = j.src + j.bstride * (int64_t)b + (size_t)r * j.ld;
+        float x[4], hi[4], lo[4];
+        if (vec_in && c0 + 3 < j.cols) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(s + c0));
+            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; u++) x[u] = (c0 + u < j.cols) ? __ldg(s + c0 + u) : 0.f;
+        }
+        split4(x, hi, lo);
+        const uint64_t o = br * j.ldo + c0;
+        *reinterpret_cast<float4*>(j.big + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(j.small + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// MN-major operand: 64 x 64 tiles transposed through shared memory; global
+// reads (along MN) and writes (along K) are 128-bit when aligned.  The loop
+// bound is the same for every thread of the block (the barriers need that).
 constexpr int TT = 64;
-__global__ void __launch_bounds__(256) split_tf32_t_kernel(const float* __restrict__ src,
-                                                           uint32_t K, uint32_t MN, uint32_t ld,
-                                                           int64_t bstride, uint32_t nb,
-                                                           uint32_t ldo, float* __restrict__ big,
-                                                           float* __restrict__ small) {
-    __shared__ float tile[TT][TT + 1];                // [k][mn]
-    const uint32_t mn0 = blockIdx.x * TT;
+__device__ __forceinline__ void split_cols(const SplitJob& j, uint32_t bid, float (*tile)[TT + 1]) {
+    const uint32_t K = j.rows, MN = j.cols;
+    const uint32_t tiles_mn = (MN + TT - 1) / TT, tiles_k = (j.ldo + TT - 1) / TT;
+    const uint64_t total = (uint64_t)tiles_mn * tiles_k * j.nb;
     const uint32_t tx = threadIdx.x & 15, ty = threadIdx.x >> 4;    // 16 x 16
-    const bool vec_in = (ld & 3u) == 0 && (bstride & 3) == 0 &&
-                        (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-    for (uint32_t b = blockIdx.z; b < nb; b += gridDim.z)
-    for (uint32_t k0 = blockIdx.y * TT; k0 < ldo; k0 += gridDim.y * TT) {
-        const float* s = src + bstride * (int64_t)b;
+    const bool vec_in = (j.ld & 3u) == 0 && (j.bstride & 3) == 0 &&
+                        (reinterpret_cast<uintptr_t>(j.src) & 15u) == 0;
+    for (uint64_t t = bid; t < total; t += j.blocks) {
+        const uint32_t mt = (uint32_t)(t % tiles_mn);
+        const uint64_t rest = t / tiles_mn;
+        const uint32_t kt = (uint32_t)(rest % tiles_k), b = (uint32_t)(rest / tiles_k);
+        const uint32_t mn0 = mt * TT, k0 = kt * TT;
+        const float* s = j.src + j.bstride * (int64_t)b;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const uint32_t kl = ty + 16 * i, k = k0 + kl, mn = mn0 + tx * 4;
             float v[4] = {0.f, 0.f, 0.f, 0.f};
             if (k < K) {
-                const float* row = s + (size_t)k * ld;
+                const float* row = s + (size_t)k * j.ld;
                 if (vec_in && mn + 3 < MN) {
                     const float4 q = __ldg(reinterpret_cast<const float4*>(row + mn));
                     v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        if (mn + j < MN) v[j] = __ldg(row + mn + j);
+                    for (int u = 0; u < 4; u++)
+                        if (mn + u < MN) v[u] = __ldg(row + mn + u);
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 4; j++) tile[kl][tx * 4 + j] = v[j];
+            for (int u = 0; u < 4; u++) tile[kl][tx * 4 + u] = v[u];
         }
         __syncthreads();
-        const size_t obase = (size_t)b * MN * ldo;
+        const size_t obase = (size_t)b * MN * j.ldo;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const uint32_t ml = ty + 16 * i, mn = mn0 + ml, k = k0 + tx * 4;
-            if (mn < MN && k < ldo) {                  // ldo % 4 == 0: k..k+3 < ldo
-                float hi[4], lo[4];
+            if (mn < MN && k < j.ldo) {                  // ldo % 4 == 0: k..k+3 < ldo
+                float x[4], hi[4], lo[4];
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float x = tile[tx * 4 + j][ml];
-                    hi[j] = rn_tf32(x);
-                    lo[j] = isfinite(hi[j]) ? rn_tf32(x - hi[j]) : 0.f;
-                }
-                const size_t o = obase + (size_t)mn * ldo + k;
-                *reinterpret_cast<float4*>(big + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<float4*>(small + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                for (int u = 0; u < 4; u++) x[u] = tile[tx * 4 + u][ml];
+                split4(x, hi, lo);
+                const size_t o = obase + (size_t)mn * j.ldo + k;
+                *reinterpret_cast<float4*>(j.big + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(j.small + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
             }
         }
         __syncthreads();
+    }
+}
+
+// The whole pre-pass of a call in one launch: blocks [0, a.blocks) split A,
+// the rest split B.
+__global__ void __launch_bounds__(256) split_tf32_kernel(const SplitJob a, const SplitJob b) {
+    __shared__ float tile[TT][TT + 1];                // [k][mn], MN-major jobs only
+    const bool first = blockIdx.x < a.blocks;
+    const uint32_t bid = first ? blockIdx.x : blockIdx.x - a.blocks;
+    if (first) {
+        if (a.mn_major) split_cols(a, bid, tile);
+        else split_rows(a, bid);
+    } else {
+        if (b.mn_major) split_cols(b, bid, tile);
+        else split_rows(b, bid);
     }
 }
 
@@ -885,7 +920,8 @@ bool reg_split_fits() {
 // One CTA per SM (persistent over `units` work units), or for PAIR one 2-CTA
 // cluster per pair of SMs, as many clusters as the device can hold at once.
 template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
-cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cudaStream_t s) {
+cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cudaStream_t s,
+                        bool pdl) {
     using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
     auto kern = umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
     static std::atomic<uint64_t> attr_done{0};     // one bit per device
@@ -921,24 +957,30 @@ cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cuda
         }
         attr_done.fetch_or(bit);
     }
-    if (!PAIR) {
-        const uint32_t grid = units < (uint32_t)num_sms ? units : (uint32_t)num_sms;
-        kern<<<grid, C_::THREADS, C_::SMEM_BYTES, s>>>(prm);
-        count_launch();
-        return cudaGetLastError();
-    }
-    const uint32_t mc = (uint32_t)max_clusters[dev & 63];
-    const uint32_t clusters = units < mc ? units : mc;
+    // pdl: launched as the programmatic dependent of the kernel before it on
+    // the stream (the 3xTF32 pre-pass); see griddepcontrol.wait in the kernel.
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(C_::THREADS);
     cfg.dynamicSmemBytes = C_::SMEM_BYTES;
     cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute at[2];
+    unsigned n_at = 0;
+    if (PAIR) {
+        const uint32_t mc = (uint32_t)max_clusters[dev & 63];
+        cfg.gridDim = dim3(2 * (units < mc ? units : mc));
+        at[n_at].id = cudaLaunchAttributeClusterDimension;
+        at[n_at].val.clusterDim.x = 2; at[n_at].val.clusterDim.y = 1; at[n_at].val.clusterDim.z = 1;
+        n_at++;
+    } else {
+        cfg.gridDim = dim3(units < (uint32_t)num_sms ? units : (uint32_t)num_sms);
+    }
+    if (pdl) {
+        at[n_at].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[n_at].val.programmaticStreamSerializationAllowed = 1;
+        n_at++;
+    }
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = n_at;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
     count_launch();
     return e;
@@ -947,10 +989,10 @@ cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cuda
 template <int KIND, int BN, int STAGES, bool PAIR>
 cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, uint32_t units, int num_sms,
                           cudaStream_t s) {
-    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES, PAIR>(prm, units, num_sms, s);
-    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES, PAIR>(prm, units, num_sms, s);
-    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES, PAIR>(prm, units, num_sms, s);
-    return launch_kind<KIND, true, true, BN, STAGES, PAIR>(prm, units, num_sms, s);
+    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
+    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
+    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
+    return launch_kind<KIND, true, true, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
 }
 
 // The reduce of split tiles, launched so that it may become resident while
@@ -1150,6 +1192,8 @@ UmmaPlan umma_plan(const GemmProblem& p, int num_sms, bool allow_wide) {
     r.kblocks = (q.K + bk - 1) / bk;
     r.kblocks_per_split = pl.kb_per;
     r.partial_bytes = pl.s > 1 ? (uint64_t)pl.partial_bytes : 0u;
+    r.too_many_tiles = (uint64_t)((q.M + ks.bm_tile - 1) / ks.bm_tile) * ((q.N + ks.BN - 1) / ks.BN) *
+                           q.batch >= (1ull << 31);
     return r;
 }
 
@@ -1193,6 +1237,7 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     // 256-row tiles on CTA pairs when no split is planned and M fills them.
     const SplitPlan pl = plan_split(ks, num_sms);
     const bool pair = ks.pair;
+    bool pdl = false;                           // the GEMM follows the 3xTF32 pre-pass
     const uint32_t bn_cta = pair ? (uint32_t)BN / 2 : (uint32_t)BN;      // B rows per CTA
 
     auto box_for = [&](const Operand& o, uint32_t tile_rows, uint32_t& bi, uint32_t& bo) {
@@ -1230,27 +1275,34 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
             !make_tmap(&prm.tmB[0], dt, 4, b_big, plane_k(b), br, ldb_o, b.nb, sb_o, BK, bn_cta) ||
             !make_tmap(&prm.tmB[1], dt, 4, b_small, plane_k(b), br, ldb_o, b.nb, sb_o, BK, bn_cta))
             return cudaErrorNotSupported;
-        auto split = [&](const Operand& o, uint32_t ldo, float* big, float* small) {
-            if (!o.mn_major) {
-                const uint64_t work = o.nb * o.outer * (ldo / 4);
-                const int threads = 256;
-                const uint64_t want = (work + threads - 1) / threads;
-                const int blocks = (int)(want < (uint64_t)num_sms * 16 ? want : (uint64_t)num_sms * 16);
-                split_tf32_kernel<<<blocks > 0 ? blocks : 1, threads, 0, s>>>(
-                    reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
-                    (uint32_t)o.ld, (int64_t)o.bstride, (uint32_t)o.nb, ldo, big, small);
-            } else {
-                const uint64_t ktiles = (o.outer + TT - 1) / TT;     // the kernel strides beyond
-                dim3 grid((uint32_t)((o.inner + TT - 1) / TT), (uint32_t)(ktiles < 65535 ? ktiles : 65535),
-                          (uint32_t)(o.nb < 65535 ? o.nb : 65535));
-                split_tf32_t_kernel<<<grid, 256, 0, s>>>(
-                    reinterpret_cast<const float*>(o.base), (uint32_t)o.outer, (uint32_t)o.inner,
-                    (uint32_t)o.ld, (int64_t)o.bstride, (uint32_t)o.nb, ldo, big, small);
-            }
-            count_launch();
+        // One launch splits both operands; the GEMM below is its programmatic
+        // dependent (its producer waits in griddepcontrol.wait before the first
+        // load of a plane), so the GEMM's launch and set-up overlap the
+        // pre-pass's last blocks.
+        auto job = [&](const Operand& o, uint32_t ldo, float* big, float* small) {
+            SplitJob j;
+            j.src = reinterpret_cast<const float*>(o.base);
+            j.rows = (uint32_t)o.outer;
+            j.cols = (uint32_t)o.inner;
+            j.ld = (uint32_t)o.ld;
+            j.bstride = (int64_t)o.bstride;
+            j.nb = (uint32_t)o.nb;
+            j.ldo = ldo;
+            j.big = big;
+            j.small = small;
+            j.mn_major = o.mn_major ? 1u : 0u;
+            // about 16 blocks of work per SM, each striding over the rest
+            const uint64_t work = o.mn_major
+                ? (uint64_t)((o.inner + TT - 1) / TT) * ((ldo + TT - 1) / TT) * o.nb
+                : (o.nb * o.outer * (ldo / 4) + 255) / 256;
+            const uint64_t cap = (uint64_t)num_sms * 16;
+            j.blocks = (uint32_t)(work < 1 ? 1 : work < cap ? work : cap);
+            return j;
         };
-        split(a, lda_o, a_big, a_small);
-        split(b, ldb_o, b_big, b_small);
+        const SplitJob ja = job(a, lda_o, a_big, a_small), jb = job(b, ldb_o, b_big, b_small);
+        split_tf32_kernel<<<ja.blocks + jb.blocks, 256, 0, s>>>(ja, jb);
+        count_launch();
+        pdl = true;
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -1300,10 +1352,10 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
                        : launch_majors<K_BF16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_F32:   // planes are K-major whatever op(A), op(B) are
-            e = !pair ? launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32, false>(prm, units, num_sms, s)
+            e = !pair ? launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32, false>(prm, units, num_sms, s, pdl)
                 : BN == BN_TF32W
-                    ? launch_kind<K_TF32X3, false, false, BN_TF32W, STAGES_TF32W, true>(prm, units, num_sms, s)
-                    : launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32P, true>(prm, units, num_sms, s);
+                    ? launch_kind<K_TF32X3, false, false, BN_TF32W, STAGES_TF32W, true>(prm, units, num_sms, s, pdl)
+                    : launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32P, true>(prm, units, num_sms, s, pdl);
             break;
         default: return cudaErrorInvalidValue;
     }
