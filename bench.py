@@ -171,6 +171,39 @@ def secondary_results(vk, hb, torch, peaks, ceil=None):
     g = torch.Generator(device="cuda").manual_seed(3)
     with hb.Handle() as h, torch.cuda.stream(s):
         h.set_stream(s)
+        # config 4 first, before the long compute-bound GEMMs below leave the GPU
+        # under its power cap: decode GEMV, 4 rotating weight sets (470 MB > L2).  Timed two
+        # ways: back-to-back calls (includes each call's launch gap) and a CUDA
+        # graph of 40 calls replayed (kernel time; what a decode loop captures).
+        K, O = 4096, 14336
+        Ws = [(torch.randn(O, K, device="cuda", generator=g) * 0.02).half() for _ in range(4)]
+        for M in (1, 4, 16):
+            X = torch.randn(M, K, device="cuda", generator=g).half()
+            C = torch.empty(M, O, device="cuda", dtype=torch.float16)
+
+            def run(i, M=M, X=X, C=C):
+                vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,
+                                     Ws[i % 4].data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
+                                     vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F, O,
+                                     vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
+            for i in range(4):
+                run(i)
+            ms = _time_loop(run, 40, s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(40):
+                    run(i)
+            graph.replay()
+            ms_g = _time_loop(lambda i: graph.replay(), 5, s) / 40
+            del graph
+            nbytes = 2.0 * (O * K + M * K + M * O)
+            gbs, gbs_g = nbytes / ms / 1e6, nbytes / ms_g / 1e6
+            out[f"gemv_m{M}"] = {"gbs": round(gbs, 1), "us": round(ms * 1e3, 2),
+                                 "gbs_graph": round(gbs_g, 1), "us_graph": round(ms_g * 1e3, 2),
+                                 "path": vk.PATH_NAMES[vk.last_path()],
+                                 "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                                 "frac_of_hbm_graph": round(gbs_g / peaks["hbm_gbs"], 4)}
+        del Ws
         # config 2, second kernel: the exact FFMA SIMT SGEMM at 4096^3 NN (two
         # input sets of 128 MiB, larger than L2, alternated call by call)
         n = 4096
@@ -220,38 +253,6 @@ def secondary_results(vk, hb, torch, peaks, ceil=None):
             if f16_ceil:
                 out[f"hgemm_tn_{n}"]["frac_of_f16_mma_measured"] = round(tf / f16_ceil, 4)
             del sets
-        # config 4: decode GEMV, 4 rotating weight sets (470 MB > L2).  Timed two
-        # ways: back-to-back calls (includes each call's launch gap) and a CUDA
-        # graph of 40 calls replayed (kernel time; what a decode loop captures).
-        K, O = 4096, 14336
-        Ws = [(torch.randn(O, K, device="cuda", generator=g) * 0.02).half() for _ in range(4)]
-        for M in (1, 4, 16):
-            X = torch.randn(M, K, device="cuda", generator=g).half()
-            C = torch.empty(M, O, device="cuda", dtype=torch.float16)
-
-            def run(i, M=M, X=X, C=C):
-                vk.lib.hipblasGemmEx(h.h, vk.HIPBLAS_OP_T, vk.HIPBLAS_OP_N, O, M, K, al,
-                                     Ws[i % 4].data_ptr(), vk.HIPBLAS_R_16F, K, X.data_ptr(),
-                                     vk.HIPBLAS_R_16F, K, be, C.data_ptr(), vk.HIPBLAS_R_16F, O,
-                                     vk.HIPBLAS_COMPUTE_32F, vk.HIPBLAS_GEMM_DEFAULT)
-            for i in range(4):
-                run(i)
-            ms = _time_loop(run, 40, s)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=s):
-                for i in range(40):
-                    run(i)
-            graph.replay()
-            ms_g = _time_loop(lambda i: graph.replay(), 5, s) / 40
-            del graph
-            nbytes = 2.0 * (O * K + M * K + M * O)
-            gbs, gbs_g = nbytes / ms / 1e6, nbytes / ms_g / 1e6
-            out[f"gemv_m{M}"] = {"gbs": round(gbs, 1), "us": round(ms * 1e3, 2),
-                                 "gbs_graph": round(gbs_g, 1), "us_graph": round(ms_g * 1e3, 2),
-                                 "path": vk.PATH_NAMES[vk.last_path()],
-                                 "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
-                                 "frac_of_hbm_graph": round(gbs_g / peaks["hbm_gbs"], 4)}
-        del Ws
         # config 5: strided-batched 256 x 2048^3 NN
         b, n = 256, 2048
         A = (torch.randn(b, n, n, device="cuda", generator=g) * 0.02).half()
@@ -637,12 +638,26 @@ def run_case(a) -> int:
         ms = e0.elapsed_time(e1) / (reps * max(1, a.iters))
         del graph
     else:
+        kev = []
+        if a.kernel_events:      # the library's event pair around each call's main kernel
+            kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(a.iters)]
+            for x, y in kev:
+                x.record(s)
+                y.record(s)
+            torch.cuda.synchronize()
         e0.record(s)
-        for _ in range(a.iters):
+        for i in range(a.iters):
+            if kev:
+                vk.set_kernel_events(*kev[i])
             call()
         e1.record(s)
         torch.cuda.synchronize()
+        vk.set_kernel_events(None, None)
         ms = e0.elapsed_time(e1) / max(1, a.iters)
+        if kev:
+            kms = sum(x.elapsed_time(y) for x, y in kev) / len(kev)
+            print(f"kernel events: {kms * 1e3:.2f} us/call between the events")
     st = vk.device_status(True)
     line = f"{a.case}: {ms * 1e3:.2f} us/call, {flop / ms / 1e9:.2f} TFLOP/s"
     if nbytes:
@@ -738,6 +753,8 @@ def main() -> int:
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--path", default="auto", choices=["auto", "simt", "tc", "gemv"],
                     help="--case: force a kernel family (vkblas_b200_set_path)")
+    ap.add_argument("--kernel-events", action="store_true",
+                    help="--case: record the library's kernel events around every call")
     ap.add_argument("--graph", action="store_true",
                     help="--case: capture the --iters calls in a CUDA graph and time 5 replays")
     args = ap.parse_args()

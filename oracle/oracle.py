@@ -24,8 +24,10 @@ _i, _u32, _i64, _f, _d, _sz = C.c_int, C.c_uint32, C.c_int64, C.c_float, C.c_dou
 
 
 def build() -> None:
-    """Compile liboracle.so (and _ref/libvkref.so when the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    """Compile liboracle.so (and _ref/libvkref.so when $VKBLAS_REFERENCE_DIR names
+    the reference tree)."""
+    ref = os.environ.get("VKBLAS_REFERENCE_DIR", "")
+    subprocess.run(["make", "-s", "-C", _HERE, "REFERENCE_DIR=" + ref], check=True)
 
 
 def _load():

@@ -1,8 +1,8 @@
 """Generate the golden fixtures that pin the oracle to the reference's own code.
 
-Run in a container that has the reference tree (it builds ``oracle/_ref``):
+Run where the reference tree exists (it builds ``oracle/_ref`` from it):
 
-    python tests/golden/gen_golden.py
+    VKBLAS_REFERENCE_DIR=/path/to/vkblas python tests/golden/gen_golden.py
 
 Outputs (committed, about 1 MB):
 
