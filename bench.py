@@ -861,21 +861,27 @@ def main() -> int:
 
     # e2e through the public ABI with host buffers: every step copies its A and
     # B from pinned host memory, calls hipblasSgemm and copies its C back, all
-    # inside the timed region.  Steps alternate between two streams, each with
+    # inside the timed region.  Steps rotate over E2E_STREAMS streams, each with
     # its own device buffers and hipBLAS handle, so a step's host-to-device
-    # copies overlap the previous step's GEMM and device-to-host copy (PCIe is
+    # copies overlap earlier steps' GEMMs and device-to-host copies (PCIe is
     # full duplex) -- how a caller streaming GEMMs through host memory runs it.
+    # With two streams a step's upload could wait for the download two steps
+    # back on its stream; three keep the upload direction busy.
+    E2E_STREAMS = 3
     hA = torch.randn(MNK * MNK, generator=torch.Generator().manual_seed(7)).pin_memory()
     hB = torch.randn(MNK * MNK, generator=torch.Generator().manual_seed(8)).pin_memory()
-    hCs = [torch.empty(MNK * MNK).pin_memory() for _ in range(2)]
-    e2e_streams = [torch.cuda.Stream() for _ in range(2)]
-    e2e_handles = [hb.Handle() for _ in range(2)]
+    hCs = [torch.empty(MNK * MNK).pin_memory() for _ in range(E2E_STREAMS)]
+    e2e_sets = sets + [(torch.empty(MNK * MNK, device="cuda"), torch.empty(MNK * MNK, device="cuda"),
+                        torch.empty(MNK * MNK, device="cuda"))
+                       for _ in range(E2E_STREAMS - len(sets))]
+    e2e_streams = [torch.cuda.Stream() for _ in range(E2E_STREAMS)]
+    e2e_handles = [hb.Handle() for _ in range(E2E_STREAMS)]
     for hh, ss in zip(e2e_handles, e2e_streams):
         hh.set_stream(ss)
 
     def e2e_step(i):
-        j = i % 2
-        dA, dB, dC = sets[j]
+        j = i % E2E_STREAMS
+        dA, dB, dC = e2e_sets[j]
         with torch.cuda.stream(e2e_streams[j]):
             dA.copy_(hA, non_blocking=True)
             dB.copy_(hB, non_blocking=True)
@@ -937,13 +943,13 @@ def main() -> int:
         "e2e": {"value": round(e2e_val, 3), "unit": "TFLOPS",
                 "h2d_bytes_per_step": 2 * MNK * MNK * 4, "d2h_bytes_per_step": MNK * MNK * 4,
                 "ms_per_step": round(e2e_ms, 4),
-                "pipelining": "steps alternate between 2 streams: a step's H2D copies overlap "
-                              "the previous step's GEMM and D2H copy"},
+                "pipelining": f"steps rotate over {E2E_STREAMS} streams: a step's H2D copies "
+                              "overlap earlier steps' GEMMs and D2H copies"},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
         "measured_ceilings": ceil,
     }
-    del sets, hA, hB, hCs
+    del sets, e2e_sets, hA, hB, hCs
     torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, info = CpuReference().sample(8.0)

@@ -227,19 +227,20 @@ def test_gemv_edges_against_splitk_oracle(dt, shape, splitk, cuda):
 
 def _auto_gemv_split(M, N, K, sms):
     """The GEMV's automatic split-K rule: about 24 resident warps per SM (CTAs of 8
-    warps, 4 when M > 8), and for 4-warp CTAs a grid within one wave of 8 per SM."""
-    two = M > 8
-    kw = 4 if two else 8
+    warps, or 4 when M > 8 or when 8-warp CTAs would need more than one wave), and
+    for 4-warp CTAs a grid within one wave of 8 per SM."""
     ctas = (N + 15) // 16
+    kw = 4 if (M > 8 or ctas > 4 * sms) else 8
     s = 1
     while (s < 16 and ctas * s < (24 // kw) * sms and K // (2 * s) >= kw * 128
-           and (not two or ctas * 2 * s <= 8 * sms)):
+           and (kw == 8 or ctas * 2 * s <= (32 // kw) * sms)):
         s *= 2
     return s
 
 
 @pytest.mark.parametrize("shape", [(12, 4096, 14336), (16, 1024, 4096), (9, 11008, 1024),
-                                   (4, 4096, 14336), (16, 300, 2048)])
+                                   (4, 4096, 14336), (16, 300, 2048), (2, 11008, 4096),
+                                   (1, 12000, 8192)])
 def test_gemv_auto_split(shape, cuda):
     """Automatic split-K factors (M > 8 uses 4-warp CTAs) against the fp64 oracle."""
     import torch
@@ -264,8 +265,9 @@ def test_gemv_auto_split(shape, cuda):
 
 
 def test_decode_routing_large_n(cuda):
-    """9-16 tokens over >= 6 row-block CTAs per SM: the automatic path is the
-    small-M tcgen05 GEMM; an explicit GEMV split-K keeps the GEMV."""
+    """9-16 tokens over many row blocks: the automatic path is the GEMV, with or
+    without an explicit split-K; a forced tensor-core path runs the small-M
+    tcgen05 GEMM."""
     import torch
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     M, N, K = 16, 6 * sms * 16, 1024
@@ -276,15 +278,18 @@ def test_decode_routing_large_n(cuda):
                                   np.zeros(M * N, np.uint16), N)[0]
     dX, dW = dev_u16(X, 0), dev_u16(W, 0)
     vk.set_stream(torch.cuda.current_stream())
-    for splitk, path in ((0, vk.PATH_TC), (2, vk.PATH_GEMV)):
+    for splitk, forced, path in ((0, vk.PATH_AUTO, vk.PATH_GEMV), (2, vk.PATH_AUTO, vk.PATH_GEMV),
+                                 (0, vk.PATH_TC, vk.PATH_TC)):
         dC = dev_u16(np.zeros(M * N, np.uint16), 0)
         vk.set_splitk(splitk)
+        vk.set_path(forced)
         try:
             st = vk.gemm(vk.DT_F16, 0, 1, M, N, K, 1.0, dX.data_ptr(), K, dW.data_ptr(), K, 0.0,
                          dC.data_ptr(), N)
             torch.cuda.synchronize()
         finally:
             vk.set_splitk(0)
+            vk.set_path(vk.PATH_AUTO)
         assert st == vk.VKBLAS_OK
         assert vk.last_path() == path
         check_status()

@@ -191,16 +191,11 @@ vkblas_status_t run(GemmProblem& p, cudaStream_t s) {
 
     int path = 0;
     if ((forced == VKBLAS_PATH_AUTO && cfg.gemv) || forced == VKBLAS_PATH_GEMV) {
-        // With 9-16 tokens and at least 6 row-block CTAs per SM the 4-warp
-        // GEMV runs unsplit, and the small-M tcgen05 GEMM streams the weights
-        // faster (4096 -> 14336, M = 16: 23.5 against 24.0 us on three
-        // boxes).  A split-K factor set for the GEMV keeps it, and so does a
-        // configuration in which the automatic choice would not take tcgen05.
-        const bool tc_better = forced == VKBLAS_PATH_AUTO && tls.splitk == 0 &&
-                               cfg.gemv_splitk == 0 && cfg.hgemm != 1 && p.M > 8 &&
-                               (p.N + 15) / 16 >= 6u * (uint32_t)ds->num_sms &&
-                               umma_profitable(p) && umma_supported(p);
-        if (gemv_supported(p) && !tc_better) path = VKBLAS_PATH_GEMV;
+        // Every 2-byte decode shape the GEMV takes (M <= 16) runs on it.  The
+        // small-M tcgen05 GEMM was as fast at 9-16 tokens on some boxes
+        // (4096 -> 14336, M = 16: 23.2 against 23.5 us) and far slower on
+        // others (33.5 against 23.6 us); the GEMV held 23.5 us on both.
+        if (gemv_supported(p)) path = VKBLAS_PATH_GEMV;
         // fp32 decode GEMV, unless the exact FFMA kernel was asked for
         else if (gemv_f32_supported(p) && (forced == VKBLAS_PATH_GEMV || cfg.sgemm != 1))
             path = VKBLAS_PATH_GEMV;

@@ -56,6 +56,7 @@ struct GemvArgs {
     const float* d_beta;
     float* partial;                       // [splitk][M][N] fp32 (split-K only)
     unsigned* tickets;                    // [gridDim.x]   (split-K only)
+    uint32_t k_rot;                       // k-step rotation multiplier (0 = plain order)
 };
 
 template <typename T> struct Mma;
@@ -132,9 +133,15 @@ __global__ void __launch_bounds__(KW * 32) gemv_kernel(GemvArgs a) {
     float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 
-    uint32_t kb = kw0;
     // Two 64-wide chunks per step: 8 x 128-bit weight loads in flight per lane.
-    for (; kb + 2 * KCHUNK <= kw1; kb += 2 * KCHUNK) {
+    // With k_rot != 0 the steps of CTA b start at step (b * k_rot) mod nstep and
+    // wrap around, so that the CTAs do not all read the same k offset of their
+    // rows at the same time.
+    const uint32_t nstep = kw1 > kw0 ? (kw1 - kw0) / (2 * KCHUNK) : 0u;
+    const uint32_t rot = (nstep && a.k_rot) ? (blockIdx.x * a.k_rot) % nstep : 0u;
+    for (uint32_t i = 0; i < nstep; i++) {
+        const uint32_t ii = i + rot < nstep ? i + rot : i + rot - nstep;
+        const uint32_t kb = kw0 + ii * 2 * KCHUNK;
         uint4 w[2][2][2];                   // [chunk][half][row]
 #pragma unroll
         for (int c = 0; c < 2; c++)
@@ -159,7 +166,7 @@ __global__ void __launch_bounds__(KW * 32) gemv_kernel(GemvArgs a) {
     }
     // Tail: 32-wide halves; K is a multiple of 8, so each lane's 8-wide block
     // is entirely inside or entirely outside [kb, kw1).
-    for (; kb < kw1; kb += 32) {
+    for (uint32_t kb = kw0 + nstep * 2 * KCHUNK; kb < kw1; kb += 32) {
         const uint32_t k = kb + 8 * t;
         const bool in = k < kw1;
         uint4 wl = (in && r0ok) ? ldg_stream(w0p + k) : z;
@@ -280,6 +287,22 @@ int gemv_warps(const GemmProblem& p, int splitk, int num_sms) {
     return ctas > 4ull * (uint64_t)num_sms ? 4 : 8;
 }
 
+// k-step rotation multiplier of the GEMV (VKBLAS_GEMV_KROT=n; 0 = plain order).
+// In plain order all CTAs read the same k offset of their rows at the same
+// time, and the HBM channels are unevenly loaded (ncu at M = 16: idlest
+// channel 26.9% active, average 51.0%).  Measured on B200 at 4096 -> 14336
+// (graph replay, one box): M = 1 22.3 -> 20.8 us, M = 8 22.65 -> 21.2 us,
+// M = 16 23.8 -> 23.35 us with multiplier 3; multipliers 1, 5 and 7 gave the
+// same within 0.1 us.
+uint32_t gemv_k_rot() {
+    static const uint32_t r = [] {
+        const char* e = getenv("VKBLAS_GEMV_KROT");
+        const int v = e ? atoi(e) : 3;
+        return (uint32_t)(v < 0 ? 0 : v);
+    }();
+    return r;
+}
+
 int device_sms() {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -312,6 +335,7 @@ cudaError_t launch_segments(const GemmProblem& p, int splitk, float* partial, un
     a.alpha = p.alpha; a.beta = p.beta; a.d_alpha = p.d_alpha; a.d_beta = p.d_beta;
     a.partial = segs > 1 ? partial : nullptr;
     a.tickets = segs > 1 ? tickets : nullptr;
+    a.k_rot = gemv_k_rot();
     dim3 grid((p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA, segs);
     const bool two = p.M > 8;
     const int kw = gemv_warps(p, (int)segs, device_sms());
@@ -333,19 +357,17 @@ bool gemv_supported(const GemmProblem& p) {
 int gemv_auto_splitk(const GemmProblem& p, int num_sms) {
     // The warps of a CTA already split K; cut K across CTAs too only when
     // there are too few row blocks to keep every SM busy: aim at 24 resident
-    // warps per SM (3 CTAs of 8 warps, or 6 of 4 when M > 8).  The 4-warp
-    // kernel (64 registers: 8 CTAs per SM) also keeps the grid within one
-    // wave.  Measured at M = 16 against the 8-warp target alone:
+    // warps per SM (3 CTAs of 8 warps, or 6 of 4).  4-warp CTAs (8 per SM)
+    // also keep the grid within one wave.  Measured at M = 16 against the 8-warp target alone:
     // 4096 rows x K = 14336 32.6 -> 24.3 us, 4096 x 4096 13.4 -> 12.1 us;
     // without the wave cap 11008 x 4096 went from 20.5 to 26.4 us.
-    const bool two = p.M > 8;
     const uint32_t kw = (uint32_t)gemv_warps(p, 1, num_sms);
     const uint32_t target = (24u / kw) * (uint32_t)num_sms;
-    const uint32_t wave = 8u * (uint32_t)num_sms;
+    const uint32_t wave = (32u / kw) * (uint32_t)num_sms;     // resident CTAs, all SMs
     const uint32_t ctas = (p.N + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
     int s = 1;
     while (s < 16 && ctas * s < target && p.K / (2u * s) >= kw * 128u &&
-           (!two || ctas * 2u * s <= wave))
+           (kw == 8 || ctas * 2u * s <= wave))
         s *= 2;
     return s;
 }

@@ -83,6 +83,7 @@ struct __align__(64) UmmaParams {
     uint32_t k_rot_mul;
     uint64_t wait_limit_ns;      // bound of every mbarrier wait
     uint32_t test_skip_first_load;   // test hook: the first stage is never filled
+    uint32_t mma_group;          // stages the MMA issuer takes at a time; 0 = Cfg::MMA_GROUP
 };
 
 template <int KIND> struct OutT;
@@ -234,6 +235,14 @@ struct Cfg {
     // for a pair, on the even CTA's barrier).
     static constexpr uint32_t TEMPTY_COUNT = (PAIR ? 2u : 1u) * 32u * EPI_WARPS;
     static constexpr uint32_t SLAB = BK * ROW_BYTES;  // MN-major: one 128-byte-wide slab
+    // Stages the MMA issuer takes at a time (wait for all, one fence, all their
+    // MMAs, one commit each).  Each stage costs a fixed 80-90 tensor cycles on
+    // top of its MMAs, so rings deep enough to spare a stage of look-ahead take
+    // two at a time.  Measured on B200 (one box, G = 1 -> 2): fp16 pair HGEMM
+    // 4096^3 128.7 -> 117.8 us, 8192^3 915 -> 865 us, 256 x 2048^3 batched
+    // 3928 -> 3715 us, small-M decode M = 16 33.5 -> 31.5 us; the 3-stage
+    // 3xTF32 ring went 541 -> 703 us, so it keeps 1.
+    static constexpr uint32_t MMA_GROUP = STAGES >= 6 ? 2u : 1u;
     static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
     static_assert(SEG_KB == 0 || EPI_COLS <= 128, "segmented epilogue keeps EPI_COLS fp32 sums per thread");
     static_assert(!REG_SPLIT || (REGS_LOW % 8 == 0 && REGS_HIGH % 8 == 0 && REGS_LOW >= 24 &&
@@ -425,14 +434,29 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                         const uint32_t d = tmem_base + buf * BN;
                         const uint32_t kb0 = ukb0 + sg * seg_kb;
                         const uint32_t kb1 = min(ukb1, kb0 + seg_kb);
-                        for (uint32_t kb = kb0; kb < kb1; kb++) {
-                            if (!wait_bar(full_bar(stage), phase, abort_flag, p.status, DS_TIMEOUT_MMA,
-                                          p.wait_limit_ns)) {
-                                ok = false;
-                                break;
+                        // Stages are taken p.mma_group at a time: wait for all of
+                        // them, one fence, all their MMAs, then one commit each.
+                        for (uint32_t kb = kb0; kb < kb1;) {
+                            // at most STAGES: a group waits on distinct stages
+                            const uint32_t grp = p.mma_group ? p.mma_group : C_::MMA_GROUP;
+                            const uint32_t gn = min(min(grp, (uint32_t)STAGES), kb1 - kb);
+                            uint32_t st = stage, ph = phase;
+                            for (uint32_t i = 0; i < gn; i++) {
+                                if (!wait_bar(full_bar(st), ph, abort_flag, p.status, DS_TIMEOUT_MMA,
+                                              p.wait_limit_ns)) {
+                                    ok = false;
+                                    break;
+                                }
+                                if (++st == STAGES) {
+                                    st = 0;
+                                    ph ^= 1u;
+                                }
                             }
+                            if (!ok) break;
                             tc_fence_after();
-                            const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
+                            st = stage;
+                            for (uint32_t i = 0; i < gn; i++) {
+                            const uint32_t sA = sbase + st * C_::STAGE_BYTES;
                             const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
 #pragma unroll
                             for (int j = 0; j < C_::KSTEPS; j++) {
@@ -446,7 +470,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                                                                     C_::SLAB, 1024)
                                                   : smem_desc_sw128(sB + pl * C_::B_PLANE + j * 32, 16, 1024);
                                 }
-                                const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
+                                const uint32_t first = (kb + i == kb0 && j == 0) ? 0u : 1u;
                                 if constexpr (KIND == K_TF32X3) {
                                     if constexpr (PAIR) {
                                         mma_tf32_pair(d, ad[1], bd[0], C_::IDESC, first);
@@ -462,12 +486,17 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                                     else mma_f16(d, ad[0], bd[0], C_::IDESC, first);
                                 }
                             }
-                            if constexpr (PAIR) tc_commit_pair_mc(empty_bar(stage), 0x3);   // both CTAs' stage
-                            else tc_commit(empty_bar(stage));
-                            if (++stage == STAGES) {
-                                stage = 0;
-                                phase ^= 1u;
+                            if (++st == STAGES) st = 0;
                             }
+                            for (uint32_t i = 0; i < gn; i++) {
+                                if constexpr (PAIR) tc_commit_pair_mc(empty_bar(stage), 0x3);   // both CTAs' stage
+                                else tc_commit(empty_bar(stage));
+                                if (++stage == STAGES) {
+                                    stage = 0;
+                                    phase ^= 1u;
+                                }
+                            }
+                            kb += gn;
                         }
                         if (!ok) break;
                         if constexpr (PAIR) tc_commit_pair_mc(tfull_bar(buf), 0x3);    // both epilogues
@@ -1023,6 +1052,17 @@ constexpr int STAGES_16P = 6, STAGES_TF32P = 4;
 // planes of 128 A rows and 128 B rows per CTA).
 constexpr int BN_TF32W = 256, STAGES_TF32W = 3;
 
+// Stages the MMA issuer takes at a time: VKBLAS_MMA_GROUP=1-4 sets it for
+// every kernel, unset (0) leaves each kernel's own (Cfg::MMA_GROUP).
+uint32_t mma_group() {
+    static const uint32_t g = [] {
+        const char* e = getenv("VKBLAS_MMA_GROUP");
+        const int v = e ? atoi(e) : 0;
+        return (uint32_t)(v < 0 ? 0 : v > 4 ? 4 : v);
+    }();
+    return g;
+}
+
 // VKBLAS_TC_PAIR=0 keeps every tensor-core GEMM on single-CTA tiles.
 bool pair_enabled() {
     static const bool on = [] {
@@ -1219,6 +1259,7 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     UmmaParams prm;
     memset(&prm, 0, sizeof(prm));
     prm.wait_limit_ns = test_stall ? TEST_WAIT_LIMIT_NS : WAIT_LIMIT_NS;
+    prm.mma_group = mma_group();
     prm.test_skip_first_load = test_stall ? 1u : 0u;
     const KernelShape ks = kernel_shape(p_in);
     const GemmProblem& p = ks.q;                 // the (possibly transposed) problem run
