@@ -284,17 +284,16 @@ def _max_over_ranks(torch, dist, ms):
 
 def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
     """The sharded BASELINE configs across the ranks (device time, max over
-    ranks), each without the gather that replicates C and with it:
+    ranks), each three ways: the GEMM alone (every rank keeps its shard), the
+    GEMM followed by one all-gather that replicates C, and the fused form
+    whose epilogue stores every tile of C into all ranks' copies over NVLink
+    (replicate="p2p"; one one-element all-reduce as the rendezvous):
 
-    * config 5, 256 x 2048^3 fp16 NN strided-batched, sharded by batch: the
-      gather as one all-gather after the GEMM, and pipelined (chunks = 4:
-      point-to-point gathers of quarter shards, each on a side stream as soon
-      as its GEMM quarter is done);
-    * config 3 at 16384^3 (fp16, hipBLAS T/N) sharded by column blocks of C,
-      the gather pipelined the same way.
+    * config 5, 256 x 2048^3 fp16 NN strided-batched, sharded by batch;
+    * config 3 at 16384^3 (fp16, hipBLAS T/N) sharded by column blocks of C.
 
-    For each: the GEMM time, the time the gather adds, and which of the two
-    bounds the step."""
+    For each: the times, what replication adds over the GEMM alone, and the
+    bytes each rank must send (its shard to every other rank)."""
     from vkblas_b200 import shard
     out = {}
 
@@ -303,6 +302,24 @@ def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
         torch.cuda.synchronize()
         dist.barrier()
         return _max_over_ranks(torch, dist, _time_loop(lambda i: run(), reps, stream))
+
+    def three_ways(run, reps, flop, C_full):
+        r = {}
+        pm = shard.PeerMap(C_full, rank, world, status_group)
+        try:
+            for key, mode in (("gemm_only", None), ("with_allgather", "gather"),
+                              ("with_p2p_epilogue", "p2p")):
+                ms = timed(lambda: run(mode, pm), reps)
+                r[key] = {"ms": round(ms, 3), "tflops": round(flop / ms / 1e9, 2)}
+        finally:
+            torch.cuda.synchronize()
+            dist.barrier()
+            pm.close()
+        base = r["gemm_only"]["ms"]
+        r["allgather_extra_ms"] = round(r["with_allgather"]["ms"] - base, 3)
+        r["p2p_extra_ms"] = round(r["with_p2p_epilogue"]["ms"] - base, 3)
+        r["p2p_over_gemm_only"] = round(r["with_p2p_epilogue"]["ms"] / base, 3)
+        return r
 
     # config 5
     b, n = 256, 2048
@@ -313,21 +330,13 @@ def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
     C_full = torch.empty(b * n * n, device="cuda", dtype=torch.float16)
     C_local = C_full[b0 * n * n: (b0 + cnt) * n * n]
 
-    def run5(gather, chunks):
+    def run5(mode, pm):
         shard.sharded_batched_gemm(vk.DT_F16, 0, 0, n, n, n, 1.0, A, n, n * n, B, n, n * n, 0.0,
                                    C_local, n, n * n, b, rank=rank, world=world,
-                                   C_full=C_full if gather else None, status_group=status_group,
-                                   chunks=chunks)
-    flop5 = b * 2.0 * n ** 3
-    r5 = {}
-    for key, gather, chunks in (("gemm_only", False, 1), ("with_allgather", True, 1),
-                                ("with_pipelined_gather", True, 4)):
-        ms = timed(lambda: run5(gather, chunks), 5)
-        r5[key] = {"ms": round(ms, 3), "tflops": round(flop5 / ms / 1e9, 2)}
-    r5["gather_ms"] = round(r5["with_allgather"]["ms"] - r5["gemm_only"]["ms"], 3)
-    r5["pipelined_extra_ms"] = round(r5["with_pipelined_gather"]["ms"] - r5["gemm_only"]["ms"], 3)
-    r5["gather_bytes_per_rank"] = (b - cnt) * n * n * 2
-    r5["bound"] = "gather" if r5["gather_ms"] > r5["gemm_only"]["ms"] else "gemm"
+                                   C_full=C_full if mode else None, status_group=status_group,
+                                   replicate=mode or "gather", peer_map=pm)
+    r5 = three_ways(run5, 5, b * 2.0 * n ** 3, C_full)
+    r5["send_bytes_per_rank"] = cnt * n * n * 2 * (world - 1)
     out["hgemm_batched_256x2048_sharded"] = r5
     del A, B, C_full, C_local
     torch.cuda.empty_cache()
@@ -341,17 +350,13 @@ def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
     C_full = torch.empty(m * nn, device="cuda", dtype=torch.float16)
     C_cols = C_full[c0 * m: (c0 + cc) * m]
 
-    def run3(gather, chunks):
+    def run3(mode, pm):
         shard.sharded_column_gemm_hip(vk.DT_F16, 1, 0, m, nn, k, 1.0, A, k, Bc, k, 0.0, C_cols, m,
-                                      rank=rank, world=world, C_full=C_full if gather else None,
-                                      status_group=status_group, chunks=chunks)
-    flop3 = 2.0 * m * nn * k
-    r3 = {}
-    for key, gather, chunks in (("gemm_only", False, 1), ("with_pipelined_gather", True, 4)):
-        ms = timed(lambda: run3(gather, chunks), 3)
-        r3[key] = {"ms": round(ms, 3), "tflops": round(flop3 / ms / 1e9, 2)}
-    r3["pipelined_extra_ms"] = round(r3["with_pipelined_gather"]["ms"] - r3["gemm_only"]["ms"], 3)
-    r3["gather_bytes_per_rank"] = (nn - cc) * m * 2
+                                      rank=rank, world=world, C_full=C_full if mode else None,
+                                      status_group=status_group, replicate=mode or "gather",
+                                      peer_map=pm)
+    r3 = three_ways(run3, 3, 2.0 * m * nn * k, C_full)
+    r3["send_bytes_per_rank"] = cc * m * 2 * (world - 1)
     out["hgemm_tn_16384_column_sharded"] = r3
     del A, Bc, C_full, C_cols
     torch.cuda.empty_cache()

@@ -67,6 +67,31 @@ vkblas_status_t vkblas_gemv_splitk_noalloc(vkblas_dtype_t dtype, uint32_t M, uin
                                            const void* W, uint32_t ldw, float beta, void* C,
                                            uint32_t ldc, uint32_t splitk, void* stream);
 
+/* Replicated-output GEMM for data-parallel sharding.  No counterpart in the
+ * reference (its engine drove one device).  Computes the engine call
+ * (dtype, op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, batch,
+ * stride_a/b/c) on the tcgen05 path, on `stream` (a cudaStream_t; NULL =
+ * legacy default stream), and writes every element of C it produces also to
+ * each of the `npeers` (0..7) buffers in peer_C, at the same element offset
+ * from peer_C[j] as from C.  peer_C[j] are addresses valid in this process
+ * (another GPU's memory mapped by CUDA IPC, over NVLink); the beta term reads
+ * only C.  The peer stores are fenced system-wide before the kernels end;
+ * the caller orders them before a peer reads its buffer with a collective
+ * on `stream` after this call (a one-element NCCL all-reduce does).
+ * VKBLAS_ERR_PARAM: unknown dtype, more than 7 peers, a null peer, or what
+ * the engine rejects.  VKBLAS_ERR_FALLBACK (nothing launched, C and the
+ * peers untouched): the problem cannot run on the tensor-core path (operand
+ * alignment; a 2-byte problem with M <= 64 and N >= 128, which runs
+ * transposed; scratch that cannot be had); the caller computes C and gathers
+ * it another way. */
+vkblas_status_t vkblas_b200_gemm_replicated(vkblas_dtype_t dtype, vkblas_op_t op_a,
+                                            vkblas_op_t op_b, uint32_t M, uint32_t N, uint32_t K,
+                                            float alpha, const void* A, uint32_t lda,
+                                            const void* B, uint32_t ldb, float beta, void* C,
+                                            uint32_t ldc, uint32_t batch, int64_t stride_a,
+                                            int64_t stride_b, int64_t stride_c,
+                                            void* const* peer_C, uint32_t npeers, void* stream);
+
 /* Stream used by the vkblas_gemm_* calls made from the calling thread
  * (thread-local; default NULL = legacy default stream). */
 void vkblas_set_stream(void* stream);

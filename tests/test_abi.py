@@ -169,6 +169,28 @@ def test_engine_validation_and_no_device():
     vk.lib.vkblas_cache_invalidate_base(None)
 
 
+def test_replicated_gemm_argument_checks_without_device_work():
+    """vkblas_b200_gemm_replicated rejects bad peer lists and problems before
+    it looks for a device (these pointers are never dereferenced)."""
+    p = 0x10000
+    n0 = vk.launch_count()
+    ok = dict(A=p, lda=64, B=p, ldb=64, C_=p, ldc=64)
+
+    def call(dtype=vk.DT_F16, M=64, N=64, K=64, peers=(p + 0x1000,), **kw):
+        a = {**ok, **kw}
+        return vk.gemm_replicated(dtype, 0, 0, M, N, K, 1.0, a["A"], a["lda"], a["B"], a["ldb"],
+                                  0.0, a["C_"], a["ldc"], list(peers))
+    assert call(peers=[p + 0x1000 * i for i in range(1, 9)]) == vk.VKBLAS_ERR_PARAM   # 8 peers
+    assert call(peers=(p, 0)) == vk.VKBLAS_ERR_PARAM                                  # a null peer
+    assert call(dtype=7) == vk.VKBLAS_ERR_PARAM                                       # dtype
+    assert call(M=0) == vk.VKBLAS_ERR_PARAM
+    assert call(C_=0) == vk.VKBLAS_ERR_PARAM
+    # a null peer array with a non-zero count
+    assert vk.lib.vkblas_b200_gemm_replicated(vk.DT_F16, 0, 0, 64, 64, 64, 1.0, p, 64, p, 64, 0.0,
+                                              p, 64, 1, 0, 0, 0, None, 1, None) == vk.VKBLAS_ERR_PARAM
+    assert vk.launch_count() == n0
+
+
 def test_engine_without_gpu_fails_loudly():
     """On a machine with no CUDA device the engine reports ERR_INIT and runs nothing."""
     torch = pytest.importorskip("torch")

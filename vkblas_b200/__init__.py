@@ -52,6 +52,10 @@ def _load() -> C.CDLL:
     lib.vkblas_gemm_ex.argtypes = [i32, i32, i32, u32, u32, u32, vp, vp, i32, vp, u32, vp, u32, vp,
                                    u32, u32, i64, i64, i64, vp]
     lib.vkblas_gemm_ex.restype = i32
+    lib.vkblas_b200_gemm_replicated.argtypes = [i32, i32, i32, u32, u32, u32, f32, vp, u32, vp,
+                                                u32, f32, vp, u32, u32, i64, i64, i64,
+                                                C.POINTER(vp), u32, vp]
+    lib.vkblas_b200_gemm_replicated.restype = i32
     lib.vkblas_gemv_splitk_noalloc.argtypes = [i32, u32, u32, u32, f32, vp, u32, vp, u32, f32, vp,
                                                u32, u32, vp]
     lib.vkblas_gemv_splitk_noalloc.restype = i32
@@ -217,6 +221,21 @@ def gemm(dtype: int, op_a: int, op_b: int, M: int, N: int, K: int, alpha: float,
     Returns the vkblas_status_t value."""
     fn = getattr(_get(), _GEMM_BY_DTYPE[dtype])
     return fn(op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C_, ldc, batch, sa, sb, sc)
+
+
+def gemm_replicated(dtype: int, op_a: int, op_b: int, M: int, N: int, K: int, alpha: float,
+                    A: int, lda: int, B: int, ldb: int, beta: float, C_: int, ldc: int,
+                    peers, batch: int = 1, sa: int = 0, sb: int = 0, sc: int = 0,
+                    stream=None) -> int:
+    """vkblas_b200_gemm_replicated on raw device pointers: the engine call,
+    with every C element also stored at the same offset from each address in
+    ``peers`` (at most 7).  ``stream``: a torch stream, a raw cudaStream_t or
+    None (legacy default stream).  Returns the vkblas_status_t value."""
+    arr = (C.c_void_p * max(1, len(peers)))(*[C.c_void_p(int(x)) for x in peers])
+    raw = getattr(stream, "cuda_stream", stream)
+    return _get().vkblas_b200_gemm_replicated(dtype, op_a, op_b, M, N, K, alpha, A, lda, B, ldb,
+                                              beta, C_, ldc, batch, sa, sb, sc, arr, len(peers),
+                                              raw)
 
 
 def dtype_of(t) -> int:

@@ -105,9 +105,14 @@ UmmaPlan umma_plan(const GemmProblem& p, int num_sms, bool allow_wide);
 // ev_start / ev_end (may be null): recorded on `s` right before the GEMM
 // kernel (after any 3xTF32 pre-pass) and right after it (after the split
 // reduce, if any) -- the measurement hook vkblas_b200_set_kernel_events.
+// peers / npeers (<= 7): pointers, valid in this process, to other copies of
+// C with C's layout; every element the kernels write to C is written to each
+// of them too (cudaErrorInvalidValue for more than 7 or a null pointer,
+// cudaErrorNotSupported for a small-M transposed problem).
 cudaError_t launch_umma_gemm(const GemmProblem& p, int num_sms, int* d_status, void* workspace,
                              void* split_workspace, bool test_stall, cudaStream_t s,
-                             cudaEvent_t ev_start = nullptr, cudaEvent_t ev_end = nullptr);
+                             cudaEvent_t ev_start = nullptr, cudaEvent_t ev_end = nullptr,
+                             void* const* peers = nullptr, uint32_t npeers = 0);
 // 2-D TMA tensor map over a 2-byte matrix [outer][inner] (row stride ld
 // elements), box [box_outer][box_inner], no swizzle.  False if the driver
 // entry point is missing or the layout cannot be described.

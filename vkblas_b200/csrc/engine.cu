@@ -502,6 +502,54 @@ VKB_EXPORT vkblas_status_t vkblas_gemm_ex(vkblas_dtype_t dtype, vkblas_op_t op_a
     return run(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Tensor-core GEMM whose epilogue also writes every C element it computes to
+// up to 7 peer copies of C (replicated output for data-parallel sharding: each
+// rank computes its shard and stores it into every rank's full buffer over
+// NVLink).  No counterpart in the reference (single device).
+VKB_EXPORT vkblas_status_t vkblas_b200_gemm_replicated(
+    vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op_t op_b, uint32_t M, uint32_t N, uint32_t K,
+    float alpha, const void* A, uint32_t lda, const void* B, uint32_t ldb, float beta, void* C,
+    uint32_t ldc, uint32_t batch, int64_t stride_a, int64_t stride_b, int64_t stride_c,
+    void* const* peer_C, uint32_t npeers, void* stream) {
+    if (dtype != VKBLAS_DT_F32 && dtype != VKBLAS_DT_F16 && dtype != VKBLAS_DT_BF16)
+        return VKBLAS_ERR_PARAM;
+    if (npeers > 7 || (npeers && !peer_C)) return VKBLAS_ERR_PARAM;
+    for (uint32_t j = 0; j < npeers; j++)
+        if (!peer_C[j]) return VKBLAS_ERR_PARAM;
+    GemmProblem p = make_problem((int)dtype, op_a, op_b, M, N, K, alpha, A, lda, B, ldb, beta, C,
+                                 ldc, batch, stride_a, stride_b, stride_c);
+    vkblas_status_t st = check_problem(p);
+    if (st != VKBLAS_OK) return st;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return VKBLAS_ERR_INIT;
+    }
+    DeviceState* ds = device_state(dev);
+    if (!ds || ds->cc_major != 10) return VKBLAS_ERR_INIT;
+    if (!umma_supported(p)) return VKBLAS_ERR_FALLBACK;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const Config& cfg = config();
+    const size_t need = umma_workspace_bytes(p);
+    void* ws = need ? workspace(ds, 1, s, need) : nullptr;
+    if (need && !ws) return VKBLAS_ERR_FALLBACK;
+    const size_t need_split = cfg.tc_split ? umma_split_workspace_bytes(p, ds->num_sms) : 0;
+    void* wsplit = need_split ? workspace(ds, 2, s, need_split) : nullptr;   // null: no split
+    cudaError_t e = launch_umma_gemm(p, ds->num_sms, ds->d_status, ws, wsplit, tls.test_stall != 0,
+                                     s, reinterpret_cast<cudaEvent_t>(tls.ev_start),
+                                     reinterpret_cast<cudaEvent_t>(tls.ev_end), peer_C, npeers);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return e == cudaErrorNotSupported ? VKBLAS_ERR_FALLBACK
+               : e == cudaErrorInvalidValue ? VKBLAS_ERR_PARAM : VKBLAS_ERR_INIT;
+    }
+    tls.last = VKBLAS_PATH_TC;
+    tls.last_split = wsplit ? umma_split_count(p, ds->num_sms) : 1;
+    tls.last_pair = umma_uses_pair(p, ds->num_sms, wsplit != nullptr) ? 1 : 0;
+    tls.last_tile_n = umma_tile_n(p);
+    return VKBLAS_OK;
+}
+
 VKB_EXPORT void vkblas_set_stream(void* stream) { tls.stream = stream; }
 VKB_EXPORT void* vkblas_get_stream(void) { return tls.stream; }
 VKB_EXPORT void vkblas_b200_set_path(int path) {

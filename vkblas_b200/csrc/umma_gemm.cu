@@ -84,7 +84,19 @@ struct __align__(64) UmmaParams {
     uint64_t wait_limit_ns;      // bound of every mbarrier wait
     uint32_t test_skip_first_load;   // test hook: the first stage is never filled
     uint32_t mma_group;          // stages the MMA issuer takes at a time; 0 = Cfg::MMA_GROUP
+    // Replicated C: every value written to C is also written, at the same
+    // element offset from C, to each of the npeers copies (other GPUs' C
+    // buffers mapped into this process; the stores cross NVLink).
+    void* peer[7];
+    uint32_t npeers;
 };
+
+template <typename V, typename T>
+__device__ __forceinline__ void put_c(const UmmaParams& p, T* c, size_t off, const V& val) {
+    *reinterpret_cast<V*>(c) = val;
+    for (uint32_t j = 0; j < p.npeers; j++)
+        *reinterpret_cast<V*>(reinterpret_cast<T*>(p.peer[j]) + off) = val;
+}
 
 template <int KIND> struct OutT;
 template <> struct OutT<K_F16> { using T = __half; };
@@ -128,9 +140,11 @@ __device__ __forceinline__ void unit_info(const UmmaParams& p, uint32_t u, uint3
     }
 }
 
+// `off`: element offset of crow from C (the same offset in every peer copy).
 template <typename T>
-__device__ __forceinline__ void store_row32(T* crow, const float (&v)[32], uint32_t ncols,
-                                            bool vec, float alpha, float beta) {
+__device__ __forceinline__ void store_row32(const UmmaParams& p, T* crow, size_t off,
+                                            const float (&v)[32], uint32_t ncols, bool vec,
+                                            float alpha, float beta) {
     if (vec && ncols == 32) {
         if constexpr (sizeof(T) == 2) {
 #pragma unroll
@@ -145,7 +159,7 @@ __device__ __forceinline__ void store_row32(T* crow, const float (&v)[32], uint3
                     const float c = (beta != 0.f) ? Elem<T>::to_f(o[i]) : 0.f;
                     w[i] = Elem<T>::from_f(epilogue(alpha, v[q * 8 + i], beta, c));
                 }
-                *reinterpret_cast<uint4*>(crow + q * 8) = out;
+                put_c(p, crow + q * 8, off + q * 8, out);
             }
         } else {
 #pragma unroll
@@ -157,7 +171,7 @@ __device__ __forceinline__ void store_row32(T* crow, const float (&v)[32], uint3
                 out.y = epilogue(alpha, v[q * 4 + 1], beta, old.y);
                 out.z = epilogue(alpha, v[q * 4 + 2], beta, old.z);
                 out.w = epilogue(alpha, v[q * 4 + 3], beta, old.w);
-                *reinterpret_cast<float4*>(crow + q * 4) = out;
+                put_c(p, crow + q * 4, off + q * 4, out);
             }
         }
     } else {
@@ -165,7 +179,7 @@ __device__ __forceinline__ void store_row32(T* crow, const float (&v)[32], uint3
         for (int i = 0; i < 32; i++) {
             if ((uint32_t)i < ncols) {
                 const float c = (beta != 0.f) ? Elem<T>::to_f(crow[i]) : 0.f;
-                crow[i] = Elem<T>::from_f(epilogue(alpha, v[i], beta, c));
+                put_c(p, crow + i, off + i, Elem<T>::from_f(epilogue(alpha, v[i], beta, c)));
             }
         }
     }
@@ -570,8 +584,8 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                             if (!IS_F32 && p.c_trans)
                                 store_col32<TOut>(cb, m, n0, p.ldc, v, min(32u, p.N - n0), alpha, beta);
                             else
-                                store_row32<TOut>(crow + n0, v, min(32u, p.N - n0), p.c_vec_ok != 0,
-                                                  alpha, beta);
+                                store_row32<TOut>(p, crow + n0, (size_t)(crow + n0 - Cbase), v,
+                                                  min(32u, p.N - n0), p.c_vec_ok != 0, alpha, beta);
                         }
                     }
                 }
@@ -619,8 +633,9 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                                 store_col32<TOut>(cb, m, n0, p.ldc, sum[c], min(32u, p.N - n0),
                                                   alpha, beta);
                             else
-                                store_row32<TOut>(crow + n0, sum[c], min(32u, p.N - n0),
-                                                  p.c_vec_ok != 0, alpha, beta);
+                                store_row32<TOut>(p, crow + n0, (size_t)(crow + n0 - Cbase),
+                                                  sum[c], min(32u, p.N - n0), p.c_vec_ok != 0,
+                                                  alpha, beta);
                         }
                     }
                 }
@@ -628,6 +643,9 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
         }
     }
 
+    // Peer stores are made visible system-wide before the grid ends, so a
+    // collective that follows on this stream (the replicas' rendezvous) orders them.
+    if (p.npeers) __threadfence_system();
     __syncthreads();
     // A pair leaves together: the issuer's last commits arrive on the other
     // CTA's barriers, and its MMAs read the other CTA's shared memory.
@@ -686,7 +704,8 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
 #pragma unroll
         for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], x[j]);
     }
-    TOut* C = reinterpret_cast<TOut*>(p.C) + p.sc * (int64_t)b;
+    TOut* const C0 = reinterpret_cast<TOut*>(p.C);
+    TOut* C = C0 + p.sc * (int64_t)b;
     if (p.c_trans) {            // lanes run along C's rows already: store directly
         const uint32_t m = mb * TILE_ROWS + cm * RC + tx;
         if (m >= p.M) return;
@@ -713,10 +732,11 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
             if (m < p.M && n < p.N) {
                 TOut* c = C + (size_t)m * p.ldc + n;
                 const float old = beta != 0.f ? Elem<TOut>::to_f(*c) : 0.f;
-                *c = Elem<TOut>::from_f(epilogue(alpha, tile[cl][rl], beta, old));
+                put_c(p, c, (size_t)(c - C0), Elem<TOut>::from_f(epilogue(alpha, tile[cl][rl], beta, old)));
             }
         }
     }
+    if (p.npeers) __threadfence_system();
 }
 
 // 3xTF32 pre-pass: x -> big = rn_tf32(x), small = rn_tf32(x - big), written as
@@ -1255,9 +1275,17 @@ size_t umma_workspace_bytes(const GemmProblem& p) {
 
 cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status, void* ws,
                              void* split_ws, bool test_stall, cudaStream_t s, cudaEvent_t ev_start,
-                             cudaEvent_t ev_end) {
+                             cudaEvent_t ev_end, void* const* peers, uint32_t npeers) {
+    // Peer copies: at most 7, none null; the transposed small-M epilogue
+    // (column stores) does not write them.
+    if (npeers > 7 || (npeers && !peers)) return cudaErrorInvalidValue;
+    for (uint32_t j = 0; j < npeers; j++)
+        if (!peers[j]) return cudaErrorInvalidValue;
+    if (npeers && small_m_swap(p_in)) return cudaErrorNotSupported;
     UmmaParams prm;
     memset(&prm, 0, sizeof(prm));
+    for (uint32_t j = 0; j < npeers; j++) prm.peer[j] = peers[j];
+    prm.npeers = npeers;
     prm.wait_limit_ns = test_stall ? TEST_WAIT_LIMIT_NS : WAIT_LIMIT_NS;
     prm.mma_group = mma_group();
     prm.test_skip_first_load = test_stall ? 1u : 0u;
