@@ -14,10 +14,17 @@ fills the peers with a NaN sentinel first and checks, through the C ABI:
 * the tile plan (CTA pairs, K splits reported by vkblas_b200_last_pair /
   last_split) is the regular call's and vkblas_b200_tc_plan's, so the cases
   cover pair, single-CTA and split-reduce epilogues;
+* the epilogue that stages C boxes in shared memory and stores them with TMA
+  gives the same bits as the one that stores straight from registers
+  (VKBLAS_EPI_TMA=0), each run in its own process;
 * a problem the replicated kernel does not take (small-M transposed) returns
   VKBLAS_ERR_FALLBACK with C and the peers untouched; more than 7 peers and a
   null peer are VKBLAS_ERR_PARAM.
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -43,6 +50,8 @@ CASES = [
     (vk.DT_F16, 0, 0, 160, 136, 128, 3, 8, 24, 2),       # batch, padded ldc, single CTAs
     (vk.DT_F32, 0, 1, 300, 200, 96, 2, 3, 5, 1),         # scalar stores (odd ldc)
     (vk.DT_F16, 1, 1, 128, 100, 64, 1, 0, 0, 1),         # scalar stores (N % 8)
+    (vk.DT_BF16, 0, 1, 200, 100, 64, 1, 4, 0, 2),        # N % 8 with aligned ldc: direct stores
+    (vk.DT_BF16, 0, 1, 200, 104, 64, 1, 8, 0, 2),        # staged boxes, ragged N chunk and M
 ]
 
 
@@ -167,3 +176,52 @@ def test_replicated_gemm_declines_and_rejects(cuda):
     for p in peers:
         assert (_bits(dtype, p) == SENTINEL[dtype]).all()
     check_status()
+
+
+_STAGED_SCRIPT = r"""
+import sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+import vkblas_b200 as vk
+from oracle import oracle as orc
+out = {}
+# dtype, op_a, op_b, M, N, K, batch, ldc, sc
+for i, (dt, oa, ob, M, N, K, batch, ldc, sc) in enumerate([
+        (vk.DT_F16, 0, 0, 512, 512, 256, 1, 512, 0),
+        (vk.DT_BF16, 0, 1, 160, 136, 128, 3, 144, 160 * 144 + 24),
+        (vk.DT_F16, 1, 0, 200, 104, 64, 1, 112, 0),
+        (vk.DT_BF16, 0, 1, 384, 640, 512, 2, 648, 384 * 648 + 8)]):
+    rng = np.random.default_rng(i)
+    kind = 1 if dt == vk.DT_BF16 else 0
+    ra, ca = (K, M) if oa else (M, K)
+    rb, cb = (N, K) if ob else (K, N)
+    sa, sb = ra * ca, rb * cb
+    A = orc.narrow(kind, rng.uniform(-1, 1, sa * batch).astype(np.float32))
+    B = orc.narrow(kind, rng.uniform(-1, 1, sb * batch).astype(np.float32))
+    C = orc.narrow(kind, rng.uniform(-1, 1, max(sc, M * ldc) * batch).astype(np.float32))
+    tdt = torch.bfloat16 if kind else torch.float16
+    d = [torch.from_numpy(x.view(np.int16)).cuda().view(tdt) for x in (A, B, C)]
+    vk.set_stream(torch.cuda.current_stream())
+    vk.set_path(vk.PATH_TC)
+    st = vk.gemm(dt, oa, ob, M, N, K, 1.25, d[0].data_ptr(), ca, d[1].data_ptr(), cb, -0.5,
+                 d[2].data_ptr(), ldc, batch, sa, sb, sc)
+    torch.cuda.synchronize()
+    assert st == vk.VKBLAS_OK and vk.last_path() == vk.PATH_TC, (i, st, vk.last_path())
+    assert vk.device_status(True) == 0
+    out[f"c{i}"] = d[2].view(torch.int16).cpu().numpy()
+np.savez(sys.argv[2], **out)
+"""
+
+
+def test_staged_epilogue_matches_direct_stores(cuda, tmp_path):
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = {}
+    for flag in ("1", "0"):
+        path = str(tmp_path / f"c_{flag}.npz")
+        r = subprocess.run([sys.executable, "-c", _STAGED_SCRIPT, root, path], capture_output=True,
+                           text=True, timeout=300, env=dict(os.environ, VKBLAS_EPI_TMA=flag))
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        res[flag] = np.load(path)
+    for k in res["1"].files:
+        assert np.array_equal(res["1"][k], res["0"][k]), f"{k}: staged and direct epilogues differ"

@@ -59,6 +59,9 @@ constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;
 struct __align__(64) UmmaParams {
     CUtensorMap tmA[2];          // [plane]; 2-byte kinds use plane 0, 3xTF32 big / small
     CUtensorMap tmB[2];
+    // C as TMA store targets (c_tma): [0] this GPU's C, [1 + j] peer j's copy.
+    // 32-row x 64-column boxes, SWIZZLE_128B, over [batch][M][N].
+    CUtensorMap tmC[8];
     void* C;
     uint32_t ldc;
     int64_t sc;
@@ -89,6 +92,9 @@ struct __align__(64) UmmaParams {
     // buffers mapped into this process; the stores cross NVLink).
     void* peer[7];
     uint32_t npeers;
+    // 1: the epilogue stages whole C boxes in shared memory and stores them
+    // with TMA (2-byte kinds whose C TMA can describe; see Cfg::EPI_STAGE).
+    uint32_t c_tma;
 };
 
 template <typename V, typename T>
@@ -202,7 +208,7 @@ __device__ __forceinline__ void store_col32(T* cb, uint32_t row, uint32_t n0, ui
     }
 }
 
-template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR, int KBS = 1>
 struct Cfg {
     static constexpr int E = (KIND == K_TF32X3) ? 4 : 2;
     static constexpr int PLANES = (KIND == K_TF32X3) ? 2 : 1;
@@ -216,7 +222,11 @@ struct Cfg {
     static constexpr int BNC = PAIR ? BN / 2 : BN;             // B rows (N) per CTA
     static constexpr uint32_t A_PLANE = BM * ROW_BYTES;
     static constexpr uint32_t B_PLANE = BNC * ROW_BYTES;
-    static constexpr uint32_t STAGE_BYTES = PLANES * (A_PLANE + B_PLANE);
+    // A stage holds KBS consecutive k-blocks (each its A and B tiles, A
+    // first), filled as one and released by one commit: the MMA issuer then
+    // waits once and commits once per 4 * KBS MMAs.
+    static constexpr uint32_t KB_BYTES = PLANES * (A_PLANE + B_PLANE);
+    static constexpr uint32_t STAGE_BYTES = KBS * KB_BYTES;
     // The tensor core's fp32 accumulation truncates, so its error grows
     // linearly with the number of accumulating MMAs (measured on B200: relative
     // error ~7e-9 * K, biased toward zero).  3xTF32 therefore accumulates each
@@ -242,7 +252,15 @@ struct Cfg {
     static constexpr int THREADS = 32 * EPI_WARP0 + 32 * EPI_WARPS;
     static constexpr uint32_t REGS_LOW = 56, REGS_HIGH = 208;
     static constexpr uint32_t TMEM_COLS = NBUF * BN;                // 512
-    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    // 2-byte tiles 128 or more wide can stage C in shared memory: each
+    // epilogue warp fills 32-row x 64-column (128-byte rows, SWIZZLE_128B)
+    // boxes, two in turn, and one lane stores each with TMA -- whole 128-byte
+    // lines, also to peer copies over NVLink, instead of one 16-byte piece of
+    // 32 different rows per store instruction.
+    static constexpr bool EPI_STAGE = KIND != K_TF32X3 && BN >= 128;
+    static constexpr uint32_t EPI_BOX = 32u * ROW_BYTES;
+    static constexpr uint32_t EPI_BYTES = EPI_STAGE ? (uint32_t)EPI_WARPS * 2u * EPI_BOX : 0u;
+    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
     static constexpr uint32_t IDESC =
         instr_desc(KIND == K_F16 ? 0u : KIND == K_BF16 ? 1u : 2u, A_MN, B_MN, BM_TILE, BN);
     // Accumulator hand-back: every epilogue thread of the CTA (of both CTAs
@@ -258,16 +276,19 @@ struct Cfg {
     // 3xTF32 ring went 541 -> 703 us, so it keeps 1.
     static constexpr uint32_t MMA_GROUP = STAGES >= 6 ? 2u : 1u;
     static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
+    static_assert(SEG_KB % KBS == 0, "a segment is whole stages");
+    static_assert(MMA_GROUP >= 1, "the issuer takes at least one stage at a time");
+    static_assert(KBS == 1 || (KIND != K_TF32X3 && SEG_KB == 0), "several k-blocks a stage: 2-byte kinds");
     static_assert(SEG_KB == 0 || EPI_COLS <= 128, "segmented epilogue keeps EPI_COLS fp32 sums per thread");
     static_assert(!REG_SPLIT || (REGS_LOW % 8 == 0 && REGS_HIGH % 8 == 0 && REGS_LOW >= 24 &&
                                  REGS_HIGH <= 256 && THREADS == 384),
                   "register split: one 128-thread warpgroup low, two high");
 };
 
-template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
-__global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREADS, 1)
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR, int KBS = 1>
+__global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::THREADS, 1)
     umma_gemm_kernel(const __grid_constant__ UmmaParams p) {
-    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>;
     using TOut = typename OutT<KIND>::T;
     constexpr uint32_t NBUF = C_::NBUF;
 
@@ -276,7 +297,8 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
     const uint32_t pad = (1024u - (raw_base & 1023u)) & 1023u;
     uint8_t* smem = smem_raw + pad;
     const uint32_t sbase = raw_base + pad;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+    const uint32_t epi_smem = sbase + STAGES * C_::STAGE_BYTES;     // 1024-aligned
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES + C_::EPI_BYTES);
     const uint32_t bar0 = smem_u32(bars);
     auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
     auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (STAGES + s); };
@@ -365,8 +387,8 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                     // would be read at the same k offset at the same time, which
                     // loads the HBM channels unevenly.
                     const uint32_t rot = (BN == 64 && p.k_rot_mul) ? (t * p.k_rot_mul) % len : 0u;
-                    for (uint32_t i = 0; i < len; i++) {
-                        const uint32_t kb = ukb0 + (i + rot < len ? i + rot : i + rot - len);
+                    for (uint32_t i = 0; i < len; i += KBS) {
+                        const uint32_t nk = min((uint32_t)KBS, len - i);   // k-blocks in this stage
                         if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, p.status,
                                       DS_TIMEOUT_PRODUCER, p.wait_limit_ns)) {
                             ok = false;
@@ -383,15 +405,19 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                             continue;
                         }
                         // The issuer expects both CTAs' bytes of a pair stage.
-                        if (issuer) mbar_arrive_expect_tx(full_bar(stage), (PAIR ? 2u : 1u) * C_::STAGE_BYTES);
-                        const uint32_t sA = sbase + stage * C_::STAGE_BYTES;
-                        const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
-                        const int32_t k0 = (int32_t)(kb * C_::BK);
+                        if (issuer)
+                            mbar_arrive_expect_tx(full_bar(stage), (PAIR ? 2u : 1u) * nk * C_::KB_BYTES);
                         auto load = [&](uint32_t dst, const CUtensorMap* m, int32_t c0, int32_t c1,
                                         int32_t c2) {
                             if constexpr (PAIR) tma_load_3d_pair(dst, m, fb, c0, c1, c2);
                             else tma_load_3d(dst, m, fb, c0, c1, c2);
                         };
+                        for (uint32_t sub = 0; sub < nk; sub++) {
+                        const uint32_t ii = i + sub;
+                        const uint32_t kb = ukb0 + (ii + rot < len ? ii + rot : ii + rot - len);
+                        const uint32_t sA = sbase + stage * C_::STAGE_BYTES + sub * C_::KB_BYTES;
+                        const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
+                        const int32_t k0 = (int32_t)(kb * C_::BK);
 #pragma unroll
                         for (int pl = 0; pl < C_::PLANES; pl++) {
                             if (!A_MN) {
@@ -410,6 +436,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                                     load(sB + pl * C_::B_PLANE + j * C_::SLAB, &p.tmB[pl],
                                          n0 + j * C_::EPB, k0, bb);
                             }
+                        }
                         }
                         issued_mask |= 1u << stage;
                         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -432,6 +459,63 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
             if (lane == 0 && issuer) {
                 uint32_t stage = 0, phase = 0, u = 0;          // u: accumulator hand-overs so far
                 bool ok = true;
+                if constexpr (KBS > 1) {
+                    // Whole units (2-byte kinds have no K segments), one stage of
+                    // KBS k-blocks at a time: one wait, one fence, 4 * KBS MMAs,
+                    // one commit.  Measured on B200: waiting for the next stage
+                    // before the current stage's last k-block instead (so that
+                    // queued MMAs cover the wait) was slower, 104.0 -> 111.2 us
+                    // at 4096^3 and 755 -> 789 us at 8192^3, as the issuer then
+                    // sometimes waits for data with MMAs still unissued.
+                    for (uint32_t w = unit0; ok && w < p.total_units; w += ustride, u++) {
+                        uint32_t t, sp, ukb0, ukb1;
+                        unit_info(p, w, t, sp, ukb0, ukb1);
+                        const uint32_t buf = u % NBUF, bph = (u / NBUF) & 1u;
+                        if (!wait_bar(tempty_bar(buf), bph ^ 1u, abort_flag, p.status, DS_TIMEOUT_MMA,
+                                      p.wait_limit_ns)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t d = tmem_base + buf * BN;
+                        const uint32_t len = ukb1 - ukb0;
+                        const uint32_t nst = (len + KBS - 1) / KBS;
+                        tc_fence_after();
+                        for (uint32_t si = 0; si < nst; si++) {
+                            const uint32_t nk = min((uint32_t)KBS, len - si * KBS);
+                            if (!wait_bar(full_bar(stage), phase, abort_flag, p.status, DS_TIMEOUT_MMA,
+                                          p.wait_limit_ns)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+#pragma unroll
+                            for (uint32_t sub = 0; sub < (uint32_t)KBS; sub++) {
+                                if (sub >= nk) break;
+                                const uint32_t sA = sbase + stage * C_::STAGE_BYTES + sub * C_::KB_BYTES;
+                                const uint32_t sB = sA + C_::A_PLANE;
+#pragma unroll
+                                for (int j = 0; j < C_::KSTEPS; j++) {
+                                    const uint64_t ad = A_MN ? smem_desc_sw128(sA + j * C_::UK * ROW_BYTES, C_::SLAB, 1024)
+                                                             : smem_desc_sw128(sA + j * 32, 16, 1024);
+                                    const uint64_t bd = B_MN ? smem_desc_sw128(sB + j * C_::UK * ROW_BYTES, C_::SLAB, 1024)
+                                                             : smem_desc_sw128(sB + j * 32, 16, 1024);
+                                    const uint32_t first = (si == 0 && sub == 0 && j == 0) ? 0u : 1u;
+                                    if constexpr (PAIR) mma_f16_pair(d, ad, bd, C_::IDESC, first);
+                                    else mma_f16(d, ad, bd, C_::IDESC, first);
+                                }
+                            }
+                            if constexpr (PAIR) tc_commit_pair_mc(empty_bar(stage), 0x3);
+                            else tc_commit(empty_bar(stage));
+                            if (++stage == STAGES) {
+                                stage = 0;
+                                phase ^= 1u;
+                            }
+                        }
+                        if (!ok) break;
+                        if constexpr (PAIR) tc_commit_pair_mc(tfull_bar(buf), 0x3);    // both epilogues
+                        else tc_commit(tfull_bar(buf));
+                    }
+                } else {
                 for (uint32_t w = unit0; ok && w < p.total_units; w += ustride) {
                     uint32_t t, sp, ukb0, ukb1;
                     unit_info(p, w, t, sp, ukb0, ukb1);
@@ -453,7 +537,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                         for (uint32_t kb = kb0; kb < kb1;) {
                             // at most STAGES: a group waits on distinct stages
                             const uint32_t grp = p.mma_group ? p.mma_group : C_::MMA_GROUP;
-                            const uint32_t gn = min(min(grp, (uint32_t)STAGES), kb1 - kb);
+                            const uint32_t gn = min(min(grp, (uint32_t)STAGES), (kb1 - kb + KBS - 1) / KBS);
                             uint32_t st = stage, ph = phase;
                             for (uint32_t i = 0; i < gn; i++) {
                                 if (!wait_bar(full_bar(st), ph, abort_flag, p.status, DS_TIMEOUT_MMA,
@@ -469,8 +553,13 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                             if (!ok) break;
                             tc_fence_after();
                             st = stage;
+                            uint32_t kk = kb;                  // first k-block of stage st
                             for (uint32_t i = 0; i < gn; i++) {
-                            const uint32_t sA = sbase + st * C_::STAGE_BYTES;
+                            const uint32_t nk = min((uint32_t)KBS, kb1 - kk);
+#pragma unroll
+                            for (uint32_t sub = 0; sub < (uint32_t)KBS; sub++) {
+                            if (sub >= nk) break;
+                            const uint32_t sA = sbase + st * C_::STAGE_BYTES + sub * C_::KB_BYTES;
                             const uint32_t sB = sA + C_::PLANES * C_::A_PLANE;
 #pragma unroll
                             for (int j = 0; j < C_::KSTEPS; j++) {
@@ -484,7 +573,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                                                                     C_::SLAB, 1024)
                                                   : smem_desc_sw128(sB + pl * C_::B_PLANE + j * 32, 16, 1024);
                                 }
-                                const uint32_t first = (kb + i == kb0 && j == 0) ? 0u : 1u;
+                                const uint32_t first = (kk + sub == kb0 && j == 0) ? 0u : 1u;
                                 if constexpr (KIND == K_TF32X3) {
                                     if constexpr (PAIR) {
                                         mma_tf32_pair(d, ad[1], bd[0], C_::IDESC, first);
@@ -500,6 +589,8 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                                     else mma_f16(d, ad[0], bd[0], C_::IDESC, first);
                                 }
                             }
+                            }
+                            kk += nk;
                             if (++st == STAGES) st = 0;
                             }
                             for (uint32_t i = 0; i < gn; i++) {
@@ -510,12 +601,13 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                                     phase ^= 1u;
                                 }
                             }
-                            kb += gn;
+                            kb = kk;
                         }
                         if (!ok) break;
                         if constexpr (PAIR) tc_commit_pair_mc(tfull_bar(buf), 0x3);    // both epilogues
                         else tc_commit(tfull_bar(buf));
                     }
+                }
                 }
                 // Never leave with MMAs in flight.
                 if constexpr (PAIR) tc_commit_pair(drain_bar);
@@ -537,6 +629,9 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
         // store out, which keeps the segment sums in registers.
         constexpr bool IS_F32 = KIND == K_TF32X3;
         TOut* Cbase = reinterpret_cast<TOut*>(p.C);
+        // This warp's two C staging boxes (EPI_STAGE) and the chunks staged so far.
+        const uint32_t epi_box0 = epi_smem + (uint32_t)(warp - C_::EPI_WARP0) * 2u * C_::EPI_BOX;
+        uint32_t kc = 0;
         uint32_t u = 0;                                       // accumulator hand-overs
         bool ok = true;
         // A split unit writes its fp32 partial tile to the workspace and no C;
@@ -570,6 +665,66 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc_fence_after();
+                if constexpr (C_::EPI_STAGE) {
+                    if (sp == NO_SPLIT && p.c_tma) {
+                        const int32_t mrow0 = (int32_t)(mb * C_::BM_TILE + rank * BM + q * 32u);
+#pragma unroll 1
+                        for (int c = 0; c < C_::EPI_COLS / 64; c++) {
+                            uint32_t r[2][32];
+                            const uint32_t ta = tmem_base + lane_off + buf * BN + col0 + c * 64;
+                            tmem_ld_32x32b_x32(ta, r[0]);
+                            tmem_ld_32x32b_x32(ta + 32, r[1]);
+                            tmem_wait_ld();
+                            const uint32_t n0 = nb * BN + col0 + c * 64;
+                            if (n0 >= p.N || (uint32_t)mrow0 >= p.M) continue;      // warp-uniform
+                            // Boxes alternate over the chunks stored: the store that read
+                            // this box two stored chunks ago must be done with it.
+                            const uint32_t box = epi_box0 + (kc++ & 1u) * C_::EPI_BOX;
+                            if (lane == 0) bulk_wait_group_read<1>();
+                            __syncwarp();
+#pragma unroll
+                            for (int g = 0; g < 8; g++) {
+                                float old[8];
+#pragma unroll
+                                for (int i = 0; i < 8; i++) old[i] = 0.f;
+                                const uint32_t n = n0 + g * 8;
+                                if (beta != 0.f && m < p.M && n < p.N) {
+                                    if (n + 8 <= p.N) {
+                                        const uint4 o = *reinterpret_cast<const uint4*>(crow + n);
+                                        const TOut* oh = reinterpret_cast<const TOut*>(&o);
+#pragma unroll
+                                        for (int i = 0; i < 8; i++) old[i] = Elem<TOut>::to_f(oh[i]);
+                                    } else {
+#pragma unroll
+                                        for (int i = 0; i < 8; i++)
+                                            if (n + i < p.N) old[i] = Elem<TOut>::to_f(crow[n + i]);
+                                    }
+                                }
+                                uint4 out;
+                                TOut* w8 = reinterpret_cast<TOut*>(&out);
+#pragma unroll
+                                for (int i = 0; i < 8; i++)
+                                    w8[i] = Elem<TOut>::from_f(epilogue(
+                                        alpha, __uint_as_float(r[g >> 2][(g & 3) * 8 + i]), beta, old[i]));
+                                // SWIZZLE_128B: 16-byte chunk g of row `lane` sits at chunk g ^ (lane % 8).
+                                st_shared_v4(box + (uint32_t)lane * ROW_BYTES + (((uint32_t)g ^ ((uint32_t)lane & 7u)) << 4), out);
+                            }
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                const int32_t bz = (int32_t)b;
+                                tma_store_3d(&p.tmC[0], box, (int32_t)n0, mrow0, bz);
+                                for (uint32_t j = 0; j < p.npeers; j++)
+                                    tma_store_3d(&p.tmC[1 + j], box, (int32_t)n0, mrow0, bz);
+                                bulk_commit_group();
+                            }
+                        }
+                        tc_fence_before();
+                        release(buf);
+                        u++;
+                        continue;
+                    }
+                }
 #pragma unroll 1
                 for (int c = 0; c < C_::EPI_COLS / 32; c++) {
                     uint32_t r[32];
@@ -641,6 +796,12 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>::THREA
                 }
             }
         }
+        // Staged C boxes: every TMA store has written its data (and stopped
+        // reading shared memory) before this CTA leaves.
+        if constexpr (C_::EPI_STAGE)
+            if (p.c_tma && lane == 0) bulk_wait_group_all();
+        (void)epi_box0;
+        (void)kc;
     }
 
     // Peer stores are made visible system-wide before the grid ends, so a
@@ -948,14 +1109,14 @@ uint64_t plane_elems(const Operand& o) { return o.nb * plane_rows(o) * rup4(plan
 // threads, cover the setmaxnreg split (warpgroup 0 at REGS_LOW, the rest at
 // REGS_HIGH).  A split larger than that allocation would leave the epilogue
 // warps' setmaxnreg.inc waiting forever, so such a kernel is never launched.
-template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR, int KBS = 1>
 bool reg_split_fits() {
-    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>;
     if constexpr (!C_::REG_SPLIT) {
         return true;
     } else {
         cudaFuncAttributes fa;
-        if (cudaFuncGetAttributes(&fa, umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES, PAIR>) !=
+        if (cudaFuncGetAttributes(&fa, umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>) !=
             cudaSuccess) {
             cudaGetLastError();
             return false;
@@ -968,18 +1129,18 @@ bool reg_split_fits() {
 
 // One CTA per SM (persistent over `units` work units), or for PAIR one 2-CTA
 // cluster per pair of SMs, as many clusters as the device can hold at once.
-template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR>
+template <int KIND, bool A_MN, bool B_MN, int BN, int STAGES, bool PAIR, int KBS = 1>
 cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cudaStream_t s,
                         bool pdl) {
-    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
-    auto kern = umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES, PAIR>;
+    using C_ = Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>;
+    auto kern = umma_gemm_kernel<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>;
     static std::atomic<uint64_t> attr_done{0};     // one bit per device
     static int max_clusters[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_done.load() & bit)) {
-        if (!reg_split_fits<KIND, A_MN, B_MN, BN, STAGES, PAIR>()) return cudaErrorNotSupported;
+        if (!reg_split_fits<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>()) return cudaErrorNotSupported;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)C_::SMEM_BYTES);
         if (e != cudaSuccess) return e;
@@ -1035,13 +1196,13 @@ cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cuda
     return e;
 }
 
-template <int KIND, int BN, int STAGES, bool PAIR>
+template <int KIND, int BN, int STAGES, bool PAIR, int KBS = 1>
 cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, uint32_t units, int num_sms,
                           cudaStream_t s) {
-    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
-    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
-    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
-    return launch_kind<KIND, true, true, BN, STAGES, PAIR>(prm, units, num_sms, s, false);
+    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
+    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
+    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
+    return launch_kind<KIND, true, true, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
 }
 
 // The reduce of split tiles, launched so that it may become resident while
@@ -1068,6 +1229,8 @@ constexpr int BN_16 = 256, STAGES_16 = 4;
 constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
 // CTA pairs (256-row tiles): half of B per CTA leaves room for deeper rings.
 constexpr int STAGES_16P = 6, STAGES_TF32P = 4;
+// fp16 / bf16 pairs with two k-blocks per stage: three 64 KB stages.
+constexpr int STAGES_16P2 = 3;
 // 3xTF32 on CTA pairs with 256 x 256 tiles: 64 KB stages (big and small
 // planes of 128 A rows and 128 B rows per CTA).
 constexpr int BN_TF32W = 256, STAGES_TF32W = 3;
@@ -1081,6 +1244,26 @@ uint32_t mma_group() {
         return (uint32_t)(v < 0 ? 0 : v > 4 ? 4 : v);
     }();
     return g;
+}
+
+// k-blocks per stage of the fp16 / bf16 pair kernel: VKBLAS_F16_KBS=1 keeps
+// six one-k-block stages (with the issuer taking two at a time), else two
+// k-blocks per stage.
+int f16_pair_kbs() {
+    static const int k = [] {
+        const char* e = getenv("VKBLAS_F16_KBS");
+        return (e && *e && atoi(e) == 1) ? 1 : 2;
+    }();
+    return k;
+}
+
+// VKBLAS_EPI_TMA=0 keeps the 2-byte epilogues on direct global stores.
+bool epi_tma_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("VKBLAS_EPI_TMA");
+        return !(e && *e && atoi(e) == 0);
+    }();
+    return on;
 }
 
 // VKBLAS_TC_PAIR=0 keeps every tensor-core GEMM on single-CTA tiles.
@@ -1167,7 +1350,13 @@ SplitPlan plan_split(const KernelShape& ks, int num_sms) {
     const uint32_t seg = is32 ? 8u : 1u;                // 3xTF32 accumulates 8-k-block segments
     // 128 x 64 small-M tiles stream weights (~0.3 us per k-block) and their
     // partial tiles are a quarter of a 128 x 256 tile's.
-    const uint32_t min_saved_kb = is32 ? 16u : (BN == (uint32_t)BN_SM ? 8u : 48u);
+    static const int min_kb_env = [] {
+        const char* e = getenv("VKBLAS_SPLIT_MIN_KB");      // tuning override
+        return e && *e ? atoi(e) : -1;
+    }();
+    const uint32_t min_saved_kb = (!is32 && BN != (uint32_t)BN_SM && min_kb_env >= 0)
+                                      ? (uint32_t)min_kb_env
+                                      : is32 ? 16u : (BN == (uint32_t)BN_SM ? 8u : 48u);
     const uint64_t T =
         (uint64_t)((p.M + ks.bm_tile - 1) / ks.bm_tile) * ((p.N + BN - 1) / BN) * p.batch;
     const uint32_t num_kb = (p.K + BK - 1) / BK;
@@ -1398,6 +1587,24 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
         prm.split_kb = prm.num_kb;
         prm.total_units = prm.total_tiles;
     }
+    // C stored from shared memory by TMA (kernels with Cfg::EPI_STAGE): C and
+    // every peer copy 16-byte aligned, rows of whole 16-byte units that do
+    // not overlap, batch entries likewise, and N a multiple of 8.  Measured
+    // on B200: a TMA store clipped at an N that ends inside a 16-byte unit
+    // still wrote the rest of that unit (the ldc padding after column N).
+    if (!is32 && !ks.c_trans && epi_tma_enabled()) {
+        const CUtensorMapDataType dt =
+            p.dtype == DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        const uint64_t nbc = p.batch > 1 ? p.batch : 1;
+        bool okc = al16(p.C) && ((uint64_t)p.ldc * 2) % 16 == 0 && p.ldc >= p.N && p.N % 8 == 0 &&
+                   (nbc == 1 || (((uint64_t)p.sc * 2) % 16 == 0 &&
+                                 (uint64_t)p.sc >= (uint64_t)p.M * p.ldc));
+        for (uint32_t j = 0; okc && j < npeers; j++) okc = al16(peers[j]);
+        okc = okc && make_tmap(&prm.tmC[0], dt, 2, p.C, p.N, p.M, p.ldc, nbc, (uint64_t)p.sc, 64, 32);
+        for (uint32_t j = 0; okc && j < npeers; j++)
+            okc = make_tmap(&prm.tmC[1 + j], dt, 2, peers[j], p.N, p.M, p.ldc, nbc, (uint64_t)p.sc, 64, 32);
+        prm.c_tma = okc ? 1u : 0u;
+    }
     prm.a_batched = a.nb > 1;
     prm.b_batched = b.nb > 1;
     prm.alpha = p.alpha; prm.beta = p.beta; prm.d_alpha = p.d_alpha; prm.d_beta = p.d_beta;
@@ -1412,11 +1619,15 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     switch (p.dtype) {
         case DT_F16:
             e = sm     ? launch_majors<K_F16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s)
+                : (pair && f16_pair_kbs() == 2)
+                    ? launch_majors<K_F16, BN_16, STAGES_16P2, true, 2>(amn, bmn, prm, units, num_sms, s)
                 : pair ? launch_majors<K_F16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
                        : launch_majors<K_F16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_BF16:
             e = sm     ? launch_majors<K_BF16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s)
+                : (pair && f16_pair_kbs() == 2)
+                    ? launch_majors<K_BF16, BN_16, STAGES_16P2, true, 2>(amn, bmn, prm, units, num_sms, s)
                 : pair ? launch_majors<K_BF16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
                        : launch_majors<K_BF16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
