@@ -1249,6 +1249,19 @@ uint32_t mma_group() {
 // k-blocks per stage of the fp16 / bf16 pair kernel: VKBLAS_F16_KBS=1 keeps
 // six one-k-block stages (with the issuer taking two at a time), else two
 // k-blocks per stage.
+// k-blocks per stage of the small-M (transposed) kernel: 2 (four 48 KB
+// stages) unless VKBLAS_SM_KBS says 1 (eight 24 KB stages) or 4 (two 96 KB).
+// Measured on B200 (4096 -> 14336, graph replay), 1 / 2 / 4: M = 16 32.8 /
+// 23.4 / 25.3 us, M = 32 33.2 / 23.9 / 25.7 us, M = 64 34.5 / 25.3 / 27.2 us.
+int small_m_kbs() {
+    static const int k = [] {
+        const char* e = getenv("VKBLAS_SM_KBS");
+        const int v = e && *e ? atoi(e) : 2;
+        return v == 1 || v == 4 ? v : 2;
+    }();
+    return k;
+}
+
 int f16_pair_kbs() {
     static const int k = [] {
         const char* e = getenv("VKBLAS_F16_KBS");
@@ -1618,14 +1631,18 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     if (ev_start) cudaEventRecord(ev_start, s);        // after the 3xTF32 pre-pass
     switch (p.dtype) {
         case DT_F16:
-            e = sm     ? launch_majors<K_F16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s)
+            e = sm     ? (small_m_kbs() == 2 ? launch_majors<K_F16, BN_SM, STAGES_SM / 2, false, 2>(amn, bmn, prm, units, num_sms, s)
+                          : small_m_kbs() == 4 ? launch_majors<K_F16, BN_SM, STAGES_SM / 4, false, 4>(amn, bmn, prm, units, num_sms, s)
+                                               : launch_majors<K_F16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s))
                 : (pair && f16_pair_kbs() == 2)
                     ? launch_majors<K_F16, BN_16, STAGES_16P2, true, 2>(amn, bmn, prm, units, num_sms, s)
                 : pair ? launch_majors<K_F16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
                        : launch_majors<K_F16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_BF16:
-            e = sm     ? launch_majors<K_BF16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s)
+            e = sm     ? (small_m_kbs() == 2 ? launch_majors<K_BF16, BN_SM, STAGES_SM / 2, false, 2>(amn, bmn, prm, units, num_sms, s)
+                          : small_m_kbs() == 4 ? launch_majors<K_BF16, BN_SM, STAGES_SM / 4, false, 4>(amn, bmn, prm, units, num_sms, s)
+                                               : launch_majors<K_BF16, BN_SM, STAGES_SM, false>(amn, bmn, prm, units, num_sms, s))
                 : (pair && f16_pair_kbs() == 2)
                     ? launch_majors<K_BF16, BN_16, STAGES_16P2, true, 2>(amn, bmn, prm, units, num_sms, s)
                 : pair ? launch_majors<K_BF16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
