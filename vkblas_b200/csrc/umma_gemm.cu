@@ -619,6 +619,10 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
         if constexpr (C_::REG_SPLIT)
             asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C_::REGS_HIGH));
         // --------------------------------------------------------- epilogue
+        // Launched as a programmatic dependent, this grid may start before the
+        // previous kernel on the stream has finished: read alpha, beta and C
+        // only after it has (as the TMA producer waits before its loads).
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         float alpha = p.alpha, beta = p.beta;
         load_scalars(p.d_alpha, p.d_beta, alpha, beta);
         const uint32_t q = (uint32_t)(warp & 3);          // TMEM lane quarter of this warp
@@ -1196,13 +1200,27 @@ cudaError_t launch_kind(const UmmaParams& prm, uint32_t units, int num_sms, cuda
     return e;
 }
 
+// 2-byte GEMMs are launched as programmatic dependents of whatever kernel
+// precedes them on the stream (VKBLAS_PDL=0: plain launches).  Their CTAs
+// may then take SMs the previous grid has left and run their prologue
+// (barriers, TMEM, tensor maps) early; every global access waits in
+// griddepcontrol.wait until the previous grid has finished.
+bool pdl_all() {
+    static const bool on = [] {
+        const char* e = getenv("VKBLAS_PDL");
+        return !(e && *e && atoi(e) == 0);
+    }();
+    return on;
+}
+
 template <int KIND, int BN, int STAGES, bool PAIR, int KBS = 1>
 cudaError_t launch_majors(bool a_mn, bool b_mn, const UmmaParams& prm, uint32_t units, int num_sms,
                           cudaStream_t s) {
-    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
-    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
-    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
-    return launch_kind<KIND, true, true, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, false);
+    const bool pdl = pdl_all();
+    if (!a_mn && !b_mn) return launch_kind<KIND, false, false, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, pdl);
+    if (!a_mn && b_mn) return launch_kind<KIND, false, true, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, pdl);
+    if (a_mn && !b_mn) return launch_kind<KIND, true, false, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, pdl);
+    return launch_kind<KIND, true, true, BN, STAGES, PAIR, KBS>(prm, units, num_sms, s, pdl);
 }
 
 // The reduce of split tiles, launched so that it may become resident while
