@@ -466,7 +466,9 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
                     // before the current stage's last k-block instead (so that
                     // queued MMAs cover the wait) was slower, 104.0 -> 111.2 us
                     // at 4096^3 and 755 -> 789 us at 8192^3, as the issuer then
-                    // sometimes waits for data with MMAs still unissued.
+                    // sometimes waits for data with MMAs still unissued.  So was
+                    // waiting for the next stage between a stage's MMAs and its
+                    // commit (100.4 -> 102.9 us and 744 -> 753 us).
                     for (uint32_t w = unit0; ok && w < p.total_units; w += ustride, u++) {
                         uint32_t t, sp, ukb0, ukb1;
                         unit_info(p, w, t, sp, ukb0, ukb1);
@@ -1381,13 +1383,7 @@ SplitPlan plan_split(const KernelShape& ks, int num_sms) {
     const uint32_t seg = is32 ? 8u : 1u;                // 3xTF32 accumulates 8-k-block segments
     // 128 x 64 small-M tiles stream weights (~0.3 us per k-block) and their
     // partial tiles are a quarter of a 128 x 256 tile's.
-    static const int min_kb_env = [] {
-        const char* e = getenv("VKBLAS_SPLIT_MIN_KB");      // tuning override
-        return e && *e ? atoi(e) : -1;
-    }();
-    const uint32_t min_saved_kb = (!is32 && BN != (uint32_t)BN_SM && min_kb_env >= 0)
-                                      ? (uint32_t)min_kb_env
-                                      : is32 ? 16u : (BN == (uint32_t)BN_SM ? 8u : 48u);
+    const uint32_t min_saved_kb = is32 ? 16u : (BN == (uint32_t)BN_SM ? 8u : 48u);
     const uint64_t T =
         (uint64_t)((p.M + ks.bm_tile - 1) / ks.bm_tile) * ((p.N + BN - 1) / BN) * p.batch;
     const uint32_t num_kb = (p.K + BK - 1) / BK;
