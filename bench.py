@@ -282,7 +282,23 @@ def _max_over_ranks(torch, dist, ms):
     return float(t.item())
 
 
-def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
+NVLINK_GBS = 770.0      # measured peer copy, GB/s per direction per GPU (this pool's B200s)
+
+
+def _fused_roofline(r, flop_per_rank, send_bytes, peak_tflops):
+    """Roofline of the fused GEMM + replication: the slower of the rank's
+    FLOPs at the bf16 burst rate and the bytes it must send over NVLink at
+    the measured peer-copy rate; frac = that time / the measured time."""
+    t_math = flop_per_rank / (peak_tflops * 1e12) * 1e3
+    t_link = send_bytes / (NVLINK_GBS * 1e9) * 1e3
+    target = max(t_math, t_link)
+    r["p2p_roofline"] = {"target_ms": round(target, 3), "bound": "nvlink" if t_link > t_math else "tensor",
+                         "math_ms": round(t_math, 3), "link_ms": round(t_link, 3),
+                         "frac": round(target / r["with_p2p_epilogue"]["ms"], 3),
+                         "peaks": f"bf16 burst {peak_tflops} TF (MEASURED_PEAKS.json), NVLink {NVLINK_GBS} GB/s"}
+
+
+def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None, peaks=None):
     """The sharded BASELINE configs across the ranks (device time, max over
     ranks), each three ways: the GEMM alone (every rank keeps its shard), the
     GEMM followed by one all-gather that replicates C, and the fused form
@@ -337,6 +353,8 @@ def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
                                    replicate=mode or "gather", peer_map=pm)
     r5 = three_ways(run5, 5, b * 2.0 * n ** 3, C_full)
     r5["send_bytes_per_rank"] = cnt * n * n * 2 * (world - 1)
+    if peaks:
+        _fused_roofline(r5, cnt * 2.0 * n ** 3, r5["send_bytes_per_rank"], peaks["bf16_tflops"])
     out["hgemm_batched_256x2048_sharded"] = r5
     del A, B, C_full, C_local
     torch.cuda.empty_cache()
@@ -357,6 +375,8 @@ def sharded_secondary(vk, torch, dist, rank, world, stream, status_group=None):
                                       peer_map=pm)
     r3 = three_ways(run3, 3, 2.0 * m * nn * k, C_full)
     r3["send_bytes_per_rank"] = cc * m * 2 * (world - 1)
+    if peaks:
+        _fused_roofline(r3, 2.0 * m * cc * k, r3["send_bytes_per_rank"], peaks["bf16_tflops"])
     out["hgemm_tn_16384_column_sharded"] = r3
     del A, Bc, C_full, C_cols
     torch.cuda.empty_cache()
@@ -968,7 +988,7 @@ def main() -> int:
     if world > 1 and not args.no_secondary:
         # every rank takes the same collective steps; an error ends the run
         result["secondary"] = sharded_secondary(vk, torch, dist, rank, world, stream,
-                                                status_group)
+                                                status_group, peaks)
         torch.cuda.empty_cache()
     h.close()
     if world > 1:
