@@ -1282,16 +1282,6 @@ int small_m_kbs() {
     return k;
 }
 
-// k-blocks per stage of the single-CTA fp16 / bf16 kernel (128 x 256 tiles):
-// VKBLAS_F16S_KBS=2 gives two 96 KB stages instead of four 48 KB ones.
-int f16_single_kbs() {
-    static const int k = [] {
-        const char* e = getenv("VKBLAS_F16S_KBS");
-        return (e && *e && atoi(e) == 2) ? 2 : 1;
-    }();
-    return k;
-}
-
 int f16_pair_kbs() {
     static const int k = [] {
         const char* e = getenv("VKBLAS_F16_KBS");
@@ -1661,7 +1651,6 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
                 : (pair && f16_pair_kbs() == 2)
                     ? launch_majors<K_F16, BN_16, STAGES_16P2, true, 2>(amn, bmn, prm, units, num_sms, s)
                 : pair ? launch_majors<K_F16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
-                : f16_single_kbs() == 2 ? launch_majors<K_F16, BN_16, STAGES_16 / 2, false, 2>(amn, bmn, prm, units, num_sms, s)
                        : launch_majors<K_F16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_BF16:
@@ -1671,7 +1660,6 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
                 : (pair && f16_pair_kbs() == 2)
                     ? launch_majors<K_BF16, BN_16, STAGES_16P2, true, 2>(amn, bmn, prm, units, num_sms, s)
                 : pair ? launch_majors<K_BF16, BN_16, STAGES_16P, true>(amn, bmn, prm, units, num_sms, s)
-                : f16_single_kbs() == 2 ? launch_majors<K_BF16, BN_16, STAGES_16 / 2, false, 2>(amn, bmn, prm, units, num_sms, s)
                        : launch_majors<K_BF16, BN_16, STAGES_16, false>(amn, bmn, prm, units, num_sms, s);
             break;
         case DT_F32:   // planes are K-major whatever op(A), op(B) are
