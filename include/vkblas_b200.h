@@ -177,6 +177,10 @@ typedef struct {
     uint32_t kblocks;            /* k-blocks per tile: K / 32 (fp32) or K / 64, rounded up */
     uint32_t kblocks_per_split;  /* k-blocks per K range of a split tile */
     uint64_t partial_bytes;      /* fp32 partial-tile scratch of the split tiles */
+    uint32_t tail_tiles;         /* tiles of the last wave run as two 256 x 128 halves each in a
+                                    second, programmatically dependent grid (2-byte pair tiles
+                                    whose last wave fills at most half the SM pairs); they
+                                    follow the full_tiles whole tiles */
 } vkblas_b200_tc_plan_t;
 vkblas_status_t vkblas_b200_tc_plan(vkblas_dtype_t dtype, vkblas_op_t op_a, vkblas_op_t op_b,
                                     uint32_t M, uint32_t N, uint32_t K, uint32_t batch,

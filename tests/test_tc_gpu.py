@@ -241,6 +241,86 @@ def test_tc_pair_wave_tail_split(dtype, cuda):
     _run(dtype, 0, 0, 256, 40, 4096, 1.0, 0.0, batch=75, split=True, pair=True)
 
 
+_TAIL_SCRIPT = r"""
+import sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+import vkblas_b200 as vk
+from oracle import oracle as orc
+out = {}
+check_oracle = sys.argv[3] == "1"
+# dtype, op_a, op_b, M, N, K, batch, A and B broadcast: 1186 pair tiles -> 1184
+# whole, 2 (batch entry 592) as halves; the second column tile holds columns
+# 256-319, so its second half lies beyond N
+for i, (dt, oa, ob, M, N, K, batch) in enumerate([
+        (vk.DT_F16, 0, 0, 256, 320, 3584, 593),
+        (vk.DT_BF16, 1, 1, 256, 320, 3584, 593)]):
+    rng = np.random.default_rng(50 + i)
+    kind = 1 if dt == vk.DT_BF16 else 0
+    ra, ca = (K, M) if oa else (M, K)
+    rb, cb = (N, K) if ob else (K, N)
+    ldc = N + 8
+    sa, sb, sc = 0, 0, M * ldc
+    A = orc.narrow(kind, rng.uniform(-1, 1, ra * ca).astype(np.float32))
+    B = orc.narrow(kind, rng.uniform(-1, 1, rb * cb).astype(np.float32))
+    C = orc.narrow(kind, rng.uniform(-1, 1, sc * batch).astype(np.float32))
+    tdt = torch.bfloat16 if kind else torch.float16
+    d = [torch.from_numpy(x.view(np.int16)).cuda().view(tdt) for x in (A, B, C)]
+    vk.set_stream(torch.cuda.current_stream())
+    vk.set_path(vk.PATH_TC)
+    st = vk.gemm(dt, oa, ob, M, N, K, 0.75, d[0].data_ptr(), ca, d[1].data_ptr(), cb, 0.5,
+                 d[2].data_ptr(), ldc, batch, sa, sb, sc)
+    torch.cuda.synchronize()
+    assert st == vk.VKBLAS_OK and vk.last_path() == vk.PATH_TC and vk.last_pair(), (i, st)
+    assert vk.device_status(True) == 0
+    got = d[2].view(torch.int16).cpu().numpy().view(np.uint16)
+    vals = orc.widen(kind, got)
+    for b in ((0, batch - 1) if check_oracle else ()):   # a whole tile's entry and the tail's
+        want = orc.hgemm_rowmajor_f64(kind, oa, ob, M, N, K, 0.75, A[b * sa:], ca, B[b * sb:], cb,
+                                      0.5, C[b * sc:], ldc)[0]
+        res = vals[b * sc: b * sc + M * ldc].reshape(M, ldc)[:, :N]
+        err = orc.rel_frobenius(res, want)
+        assert err <= (8e-3 if kind else 2e-3), (i, b, err)
+    pad = np.stack([got[b * sc: b * sc + M * ldc].reshape(M, ldc)[:, N:] for b in range(batch)])
+    pad0 = np.stack([C[b * sc: b * sc + M * ldc].reshape(M, ldc)[:, N:] for b in range(batch)])
+    assert np.array_equal(pad, pad0), "ldc padding written"
+    out[f"c{i}"] = got
+np.savez(sys.argv[2], **out)
+"""
+
+
+def test_tc_narrow_tail_matches_whole_tiles(cuda, tmp_path):
+    """The narrow tail (the last wave's tiles as two 256 x 128 halves, in a
+    second grid launched as a programmatic dependent) against the same calls
+    with whole tiles (VKBLAS_NARROW_TAIL=0 VKBLAS_TC_SPLIT=0: no K split
+    either), each in its own process: within the oracle's tolerance, padding
+    untouched, and bit for bit equal (the halves add the same products in the
+    same k order)."""
+    import os
+    import subprocess
+    import sys
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if sms != 148:
+        pytest.skip("the tail shapes are chosen for 74 SM pairs")
+    for dt, oa, ob, M, N, K, batch in ((vk.DT_F16, 0, 0, 256, 320, 3584, 593),
+                                       (vk.DT_BF16, 1, 1, 256, 320, 3584, 593)):
+        assert vk.tc_plan(dt, oa, ob, M, N, K, batch, num_sms=sms)["tail_tiles"] == 2
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = {}
+    for flag in ("1", "0"):
+        path = str(tmp_path / f"tail_{flag}.npz")
+        r = subprocess.run([sys.executable, "-c", _TAIL_SCRIPT, root, path, flag],
+                           capture_output=True,
+                           text=True, timeout=300,
+                           env=dict(os.environ, VKBLAS_NARROW_TAIL=flag, VKBLAS_TC_SPLIT=flag))
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        res[flag] = np.load(path)
+    for k in res["1"].files:
+        assert np.array_equal(res["1"][k], res["0"][k]), f"{k}: narrow tail differs from whole tiles"
+
+
 @pytest.mark.parametrize("ops", [(0, 0), (1, 1)], ids=["NN", "TT"])
 @pytest.mark.parametrize("split", [False, True], ids=["whole", "split"])
 def test_tf32_wide_pair_tiles(ops, split, cuda):

@@ -31,12 +31,18 @@ def _plan(dt, oa, ob, M, N, K, batch=1, sms=SMS, wide=True):
     # the same with 256x128 tiles: 512 tiles, 68 in the last wave, no split
     ("sgemm_4096_narrow", (F32, 0, 0, 4096, 4096, 4096, 1, SMS, False),
      dict(tile_m=256, tile_n=128, pair=1, tiles=512, full_tiles=512, splits=1, kblocks=128)),
-    # BASELINE config 3, HGEMM T/N 4096^3: the split would save 32 k-blocks, fewer than 48
+    # BASELINE config 3, HGEMM T/N 4096^3: a split would save 32 k-blocks, fewer
+    # than 48, so the 34 tiles of the last wave run whole (no narrow tail either)
     ("hgemm_4096", (F16, 1, 0, 4096, 4096, 4096),
-     dict(tile_m=256, tile_n=256, pair=1, tiles=256, full_tiles=256, splits=1, kblocks=64)),
-    # HGEMM 16384^3: 4096 pair tiles, the wave tail (26 tiles) is split in 2
+     dict(tile_m=256, tile_n=256, pair=1, tiles=256, full_tiles=256, splits=1, kblocks=64,
+          tail_tiles=0)),
+    # HGEMM 16384^3: 4096 pair tiles; where a 2-way K split of the 26 left over
+    # would pay, they run as 52 halves instead (the narrow tail)
     ("hgemm_16384", (F16, 1, 0, 16384, 16384, 16384),
-     dict(tiles=4096, full_tiles=4070, splits=2, kblocks=256, kblocks_per_split=128)),
+     dict(tiles=4096, full_tiles=4070, splits=1, kblocks=256, tail_tiles=26)),
+    # HGEMM 8192^3: 62 tiles in the last wave, more than half the pairs: whole tiles
+    ("hgemm_8192", (F16, 1, 0, 8192, 8192, 8192),
+     dict(tiles=1024, full_tiles=1024, splits=1, tail_tiles=0)),
     # one pair tile, long K: 16 K ranges of 4 k-blocks (recorded split: S = 16)
     ("hgemm_256x256x4096", (F16, 0, 1, 256, 256, 4096),
      dict(tile_m=256, tile_n=256, pair=1, tiles=1, full_tiles=0, splits=16, kblocks=64,
@@ -50,9 +56,17 @@ def _plan(dt, oa, ob, M, N, K, batch=1, sms=SMS, wide=True):
     ("decode_m16", (F16, 0, 1, 16, 14336, 4096),
      dict(tile_m=128, tile_n=64, transposed=1, pair=0, tiles=112, full_tiles=112, splits=1)),
     # BASELINE config 5, 256 x 2048^3: 16384 pair tiles; 30 left over, a split
-    # would save only 16 k-blocks
+    # would save only 16 k-blocks, so they run whole
     ("batched_256x2048", (F16, 0, 0, 2048, 2048, 2048, 256),
-     dict(tile_m=256, tile_n=256, pair=1, tiles=16384, full_tiles=16384, splits=1)),
+     dict(tile_m=256, tile_n=256, pair=1, tiles=16384, full_tiles=16384, splits=1,
+          tail_tiles=0)),
+    # 75 pair tiles of K = 4096 (the GPU wave-tail test): fewer than 8 waves,
+    # so the last one is split along K
+    ("hgemm_wave_tail", (F16, 0, 0, 256, 40, 4096, 75),
+     dict(tiles=75, full_tiles=74, splits=16, tail_tiles=0)),
+    # 1186 pair tiles (16 waves + 2) of K = 3584: the 2 left over as halves
+    ("hgemm_narrow_tail", (F16, 0, 0, 256, 320, 3584, 593),
+     dict(tiles=1186, full_tiles=1184, splits=1, tail_tiles=2)),
     # M < 256: single-CTA tiles
     ("sgemm_200x300", (F32, 0, 0, 200, 300, 136),
      dict(tile_m=128, tile_n=128, pair=0, tiles=6, splits=1)),
@@ -79,6 +93,16 @@ def _check_invariants(dt, oa, ob, M, N, K, batch, sms, wide):
     assert p["tiles"] == tiles
     assert p["kblocks"] == -(-K // (32 if dt == F32 else 64))
     workers = sms // 2 if p["pair"] else sms
+    tail = p["tail_tiles"]
+    if tail:
+        # narrow tail: 2-byte 256x256 pair tiles, 8 waves or more, a last
+        # wave that fills at most half of the SM pairs, and a K split that
+        # would have paid; no K split then
+        assert dt != F32 and p["pair"] and p["tile_n"] == 256 and not p["transposed"]
+        assert p["splits"] == 1 and p["partial_bytes"] == 0
+        assert tiles >= 8 * workers and tail == tiles % workers and 2 * tail <= workers
+        assert p["full_tiles"] == tiles - tail
+        return p
     if p["splits"] == 1:
         assert p["full_tiles"] == tiles and p["partial_bytes"] == 0
         return p
@@ -98,7 +122,7 @@ def _check_invariants(dt, oa, ob, M, N, K, batch, sms, wide):
 
 def test_invariants_over_a_seeded_sweep():
     rng = np.random.default_rng(7)
-    splits = 0
+    splits = tails = 0
     for _ in range(600):
         dt = int(rng.choice([F32, F16, BF16]))
         M = int(rng.choice([int(rng.integers(1, 65)), int(rng.integers(65, 5000))]))
@@ -109,7 +133,9 @@ def test_invariants_over_a_seeded_sweep():
         p = _check_invariants(dt, int(rng.integers(0, 2)), int(rng.integers(0, 2)), M, N, K,
                               batch, sms, bool(rng.integers(0, 2)))
         splits += p["splits"] > 1
+        tails += p["tail_tiles"] > 0
     assert splits > 50, "the sweep reaches the split rule"
+    assert tails > 5, "the sweep reaches the narrow tail"
 
 
 def test_rejects_bad_arguments():

@@ -186,7 +186,7 @@ def launch_count() -> int:
 class _TcPlan(C.Structure):
     _fields_ = [(name, C.c_uint32) for name in (
         "tile_m", "tile_n", "transposed", "pair", "tiles", "full_tiles", "splits", "kblocks",
-        "kblocks_per_split")] + [("partial_bytes", C.c_uint64)]
+        "kblocks_per_split")] + [("partial_bytes", C.c_uint64), ("tail_tiles", C.c_uint32)]
 
 
 def tc_plan(dtype: int, op_a: int, op_b: int, M: int, N: int, K: int, batch: int = 1,

@@ -96,6 +96,7 @@ struct UmmaPlan {
     uint32_t tile_m, tile_n, transposed, pair;
     uint32_t tiles, full_tiles, splits, kblocks, kblocks_per_split;
     uint64_t partial_bytes;
+    uint32_t tail_tiles;     // last-wave tiles run as two 256 x 128 halves each
     bool too_many_tiles;     // 2^31 tiles or more: the launch path rejects the call
 };
 UmmaPlan umma_plan(const GemmProblem& p, int num_sms, bool allow_wide);

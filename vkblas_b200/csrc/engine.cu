@@ -648,6 +648,7 @@ VKB_EXPORT vkblas_status_t vkblas_b200_tc_plan(vkblas_dtype_t dtype, vkblas_op_t
     out->kblocks = r.kblocks;
     out->kblocks_per_split = r.kblocks_per_split;
     out->partial_bytes = r.partial_bytes;
+    out->tail_tiles = r.tail_tiles;
     return VKBLAS_OK;
 }
 

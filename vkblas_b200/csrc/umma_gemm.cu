@@ -95,7 +95,16 @@ struct __align__(64) UmmaParams {
     // 1: the epilogue stages whole C boxes in shared memory and stores them
     // with TMA (2-byte kinds whose C TMA can describe; see Cfg::EPI_STAGE).
     uint32_t c_tma;
+    // Narrow tail (half-width launch of a 256-wide grid's last tiles): unit u
+    // is half (u & 1) of tile tail_first + (u >> 1) of the 256-wide tile grid
+    // (tiles_m x tiles_n); NO_TAIL otherwise.
+    uint32_t tail_first;
+    // 1: this grid reads nothing the previous grid writes before it ends (the
+    // narrow tail after its main launch), so it waits for that grid only at
+    // its end, and so finishes after it.
+    uint32_t dep_end;
 };
+constexpr uint32_t NO_TAIL = 0xFFFFFFFFu;
 
 template <typename V, typename T>
 __device__ __forceinline__ void put_c(const UmmaParams& p, T* c, size_t off, const V& val) {
@@ -147,6 +156,20 @@ __device__ __forceinline__ void unit_info(const UmmaParams& p, uint32_t u, uint3
 }
 
 // `off`: element offset of crow from C (the same offset in every peer copy).
+// Unit w -> its tile t (split bookkeeping), K range and C coordinates; in a
+// narrow-tail grid the column block counts BN-wide blocks of the half tiles.
+__device__ __forceinline__ void unit_coords(const UmmaParams& p, uint32_t w, uint32_t& t,
+                                            uint32_t& sp, uint32_t& kb0, uint32_t& kb1,
+                                            uint32_t& b, uint32_t& mb, uint32_t& nb) {
+    unit_info(p, w, t, sp, kb0, kb1);
+    if (p.tail_first != NO_TAIL) {
+        tile_coords(p, p.tail_first + (w >> 1), b, mb, nb);
+        nb = nb * 2u + (w & 1u);
+    } else {
+        tile_coords(p, t, b, mb, nb);
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ void store_row32(const UmmaParams& p, T* crow, size_t off,
                                             const float (&v)[32], uint32_t ncols, bool vec,
@@ -354,9 +377,6 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
     if constexpr (PAIR) cluster_sync();      // the peer's barriers are initialised
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // Let a programmatically dependent split_reduce_kernel get resident; it
-    // waits (griddepcontrol.wait) until this grid has finished and flushed.
-    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Warp roles.  With a register split, setmaxnreg opens each warpgroup's
     // branch, so that the compiler allocates each branch within its limit.
     if (warp < C_::EPI_WARP0) {
@@ -370,14 +390,18 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
                 // to finish and its writes to be visible before the first
                 // load.  Nothing else of this kernel reads memory the pre-pass
                 // writes.  Without a prerequisite grid this returns at once.
-                asm volatile("griddepcontrol.wait;" ::: "memory");
+                if (!p.dep_end) asm volatile("griddepcontrol.wait;" ::: "memory");
+                // Only now let a programmatic dependent (the next GEMM, a split
+                // reduce, a narrow tail) launch: when it starts, every grid
+                // before this one has finished, which a narrow tail relies on
+                // to read A, B and C without waiting for this grid.
+                asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
                 uint32_t stage = 0, phase = 0;
                 uint32_t issued_mask = 0, issued_parity = 0;   // per stage: issued ever / last parity
                 bool ok = true;
                 for (uint32_t u = unit0; ok && u < p.total_units; u += ustride) {
                     uint32_t t, sp, ukb0, ukb1, b, mb, nb;
-                    unit_info(p, u, t, sp, ukb0, ukb1);
-                    tile_coords(p, t, b, mb, nb);
+                    unit_coords(p, u, t, sp, ukb0, ukb1, b, mb, nb);
                     const int32_t m0 = (int32_t)(mb * C_::BM_TILE + rank * BM);
                     const int32_t n0 = (int32_t)(nb * BN + rank * C_::BNC);
                     const int32_t ba = p.a_batched ? (int32_t)b : 0, bb = p.b_batched ? (int32_t)b : 0;
@@ -624,7 +648,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
         // Launched as a programmatic dependent, this grid may start before the
         // previous kernel on the stream has finished: read alpha, beta and C
         // only after it has (as the TMA producer waits before its loads).
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (!p.dep_end) asm volatile("griddepcontrol.wait;" ::: "memory");
         float alpha = p.alpha, beta = p.beta;
         load_scalars(p.d_alpha, p.d_beta, alpha, beta);
         const uint32_t q = (uint32_t)(warp & 3);          // TMEM lane quarter of this warp
@@ -659,8 +683,7 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
         };
         for (uint32_t w = unit0; ok && w < p.total_units; w += ustride) {
             uint32_t t, sp, ukb0, ukb1, b, mb, nb;
-            unit_info(p, w, t, sp, ukb0, ukb1);
-            tile_coords(p, t, b, mb, nb);
+            unit_coords(p, w, t, sp, ukb0, ukb1, b, mb, nb);
             const uint32_t m = mb * C_::BM_TILE + rank * BM + row;
             TOut* cb = Cbase + p.sc * (int64_t)b;
             TOut* crow = cb + (size_t)m * p.ldc;
@@ -822,6 +845,9 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
         if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C_::TMEM_COLS);
         else tmem_dealloc(tmem_base, C_::TMEM_COLS);
     }
+    // A grid that skipped the wait at its start ends after its prerequisite,
+    // so work that depends on this grid also sees everything before it.
+    if (p.dep_end && threadIdx.x == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // Split tiles: C = alpha * (sum of the splits' partials in split order, fp32
@@ -1251,6 +1277,9 @@ constexpr int BN_TF32 = 128, STAGES_TF32 = 3;
 constexpr int STAGES_16P = 6, STAGES_TF32P = 4;
 // fp16 / bf16 pairs with two k-blocks per stage: three 64 KB stages.
 constexpr int STAGES_16P2 = 3;
+// Narrow tail of fp16 / bf16 pair grids: 256 x 128 tiles, four 48 KB stages of
+// two k-blocks each.
+constexpr int BN_16T = 128, STAGES_16T = 4;
 // 3xTF32 on CTA pairs with 256 x 256 tiles: 64 KB stages (big and small
 // planes of 128 A rows and 128 B rows per CTA).
 constexpr int BN_TF32W = 256, STAGES_TF32W = 3;
@@ -1373,7 +1402,17 @@ KernelShape kernel_shape(const GemmProblem& p) { return kernel_shape(p, tf32_wid
 struct SplitPlan {
     uint32_t full, s, kb_per, units;
     size_t partial_bytes;
+    uint32_t tail;       // last-wave tiles run as 256 x 128 halves in a second grid
 };
+
+// VKBLAS_NARROW_TAIL=0 keeps the last wave of fp16 / bf16 pair tiles whole.
+bool narrow_tail_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("VKBLAS_NARROW_TAIL");
+        return !(e && *e && atoi(e) == 0);
+    }();
+    return on;
+}
 
 SplitPlan plan_split(const KernelShape& ks, int num_sms) {
     const GemmProblem& p = ks.q;
@@ -1387,7 +1426,7 @@ SplitPlan plan_split(const KernelShape& ks, int num_sms) {
     const uint64_t T =
         (uint64_t)((p.M + ks.bm_tile - 1) / ks.bm_tile) * ((p.N + BN - 1) / BN) * p.batch;
     const uint32_t num_kb = (p.K + BK - 1) / BK;
-    SplitPlan pl{(uint32_t)T, 1, num_kb, (uint32_t)T, 0};
+    SplitPlan pl{(uint32_t)T, 1, num_kb, (uint32_t)T, 0, 0};
     // Workers: SMs, or SM pairs for 256-row tiles (the per-SM work of a tile
     // and its k-block time are the same in both cases).
     const int workers = ks.pair ? num_sms / 2 : num_sms;
@@ -1403,6 +1442,20 @@ SplitPlan plan_split(const KernelShape& ks, int num_sms) {
     kb_per = (kb_per + seg - 1) / seg * seg;
     const uint32_t s2 = (num_kb + kb_per - 1) / kb_per;
     if (s2 < 2 || num_kb - kb_per < min_saved_kb) return pl;
+    // Where the last wave would be split along K, 2-byte 256 x 256 pair tiles
+    // of a long grid (8 waves or more) whose last wave fills at most half of
+    // the SM pairs run as twice as many 256 x 128 halves instead, in one wave
+    // of a second grid, with no partial sums to write and add.  A half tile
+    // reads its A rows again, so it pays only where the tail is a small part
+    // of the work.  Measured on B200 against the split: 16384^3 (26 of 4096
+    // tiles) 6149 -> 5998 and 6156 -> 6048 us; 4096 x 4096 x 16384 (34 of
+    // 256) 387 -> 401 us.  Without a split neither pays: 4096^3 101.4 -> 106.1 us.
+    if (!is32 && ks.pair && !ks.c_trans && BN == 256u && T >= 8 * P && 2 * rem <= P &&
+        narrow_tail_enabled()) {
+        pl.full = pl.units = (uint32_t)(T - rem);
+        pl.tail = (uint32_t)rem;
+        return pl;
+    }
     pl.full = (uint32_t)(T - rem);
     pl.s = s2;
     pl.kb_per = kb_per;
@@ -1462,8 +1515,9 @@ UmmaPlan umma_plan(const GemmProblem& p, int num_sms, bool allow_wide) {
     r.tile_n = ks.BN;
     r.transposed = ks.c_trans ? 1u : 0u;
     r.pair = ks.pair ? 1u : 0u;
-    r.tiles = pl.s > 1 ? pl.full + (pl.units - pl.full) / pl.s : pl.units;
+    r.tiles = (pl.s > 1 ? pl.full + (pl.units - pl.full) / pl.s : pl.units) + pl.tail;
     r.full_tiles = pl.full;
+    r.tail_tiles = pl.tail;
     r.splits = pl.s;
     r.kblocks = (q.K + bk - 1) / bk;
     r.kblocks_per_split = pl.kb_per;
@@ -1500,6 +1554,7 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     if (npeers && small_m_swap(p_in)) return cudaErrorNotSupported;
     UmmaParams prm;
     memset(&prm, 0, sizeof(prm));
+    prm.tail_first = NO_TAIL;
     for (uint32_t j = 0; j < npeers; j++) prm.peer[j] = peers[j];
     prm.npeers = npeers;
     prm.wait_limit_ns = test_stall ? TEST_WAIT_LIMIT_NS : WAIT_LIMIT_NS;
@@ -1638,6 +1693,23 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     prm.status = d_status;
     prm.c_vec_ok = al16(p.C) && ((uint64_t)p.ldc * esize) % 16 == 0 &&
                    (p.batch == 1 || ((uint64_t)p.sc * esize) % 16 == 0);
+    // Narrow tail: this grid runs the whole tiles; a second grid, launched
+    // right after it as its programmatic dependent, runs the last wave's
+    // pl.tail tiles as 256 x 128 halves.  Its B tensor map has 64-row boxes.
+    UmmaParams prmT;
+    if (pl.tail) {
+        prm.full_tiles = prm.total_units = prm.total_tiles - pl.tail;
+        prmT = prm;
+        prmT.tail_first = prm.total_tiles - pl.tail;
+        prmT.full_tiles = prmT.total_units = 2 * pl.tail;
+        prmT.dep_end = 1;
+        uint32_t tbi, tbo;
+        box_for(b, BN_16T / 2, tbi, tbo);
+        const CUtensorMapDataType dt =
+            p.dtype == DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        if (!make_tmap(&prmT.tmB[0], dt, 2, b.base, b.inner, b.outer, b.ld, b.nb, b.bstride, tbi, tbo))
+            return cudaErrorNotSupported;
+    }
     const uint32_t units = prm.total_units;
     const bool amn = a.mn_major, bmn = b.mn_major;
     cudaError_t e;
@@ -1669,6 +1741,12 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
                     : launch_kind<K_TF32X3, false, false, BN_TF32, STAGES_TF32P, true>(prm, units, num_sms, s, pdl);
             break;
         default: return cudaErrorInvalidValue;
+    }
+    if (e == cudaSuccess && pl.tail) {
+        const uint32_t tu = prmT.total_units;
+        e = p.dtype == DT_F16
+                ? launch_majors<K_F16, BN_16T, STAGES_16T, true, 2>(amn, bmn, prmT, tu, num_sms, s)
+                : launch_majors<K_BF16, BN_16T, STAGES_16T, true, 2>(amn, bmn, prmT, tu, num_sms, s);
     }
     if (e == cudaSuccess && prm.split_s > 1) {
         switch (p.dtype) {
