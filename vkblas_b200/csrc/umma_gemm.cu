@@ -99,6 +99,7 @@ struct __align__(64) UmmaParams {
     // is half (u & 1) of tile tail_first + (u >> 1) of the 256-wide tile grid
     // (tiles_m x tiles_n); NO_TAIL otherwise.
     uint32_t tail_first;
+    uint32_t group_m;            // M-blocks that sweep the N-blocks together (tile order)
     // 1: this grid reads nothing the previous grid writes before it ends (the
     // narrow tail after its main launch), so it waits for that grid only at
     // its end, and so finishes after it.
@@ -123,9 +124,9 @@ __device__ __forceinline__ void tile_coords(const UmmaParams& p, uint32_t t, uin
     const uint32_t per = p.tiles_m * p.tiles_n;
     b = t / per;
     const uint32_t r = t - b * per;
-    // Groups of 8 M-blocks sweep the N-blocks together: consecutive tiles
+    // Groups of group_m M-blocks sweep the N-blocks together: consecutive tiles
     // (which run concurrently on neighbouring SMs) share A rows and B columns in L2.
-    const uint32_t G = 8;
+    const uint32_t G = p.group_m;
     const uint32_t group = r / (G * p.tiles_n);
     const uint32_t first_m = group * G;
     const uint32_t gsize = min(p.tiles_m - first_m, G);
@@ -1319,6 +1320,18 @@ int f16_pair_kbs() {
     return k;
 }
 
+// Tile order: groups of M-blocks sweep the N-blocks together, so that the
+// tiles running at the same time share A rows and B columns in L2.
+// VKBLAS_GROUP_M=n fixes the group size; 0 (unset) lets launch_umma_gemm pick.
+uint32_t group_m() {
+    static const uint32_t g = [] {
+        const char* e = getenv("VKBLAS_GROUP_M");
+        const int v = e && *e ? atoi(e) : 0;
+        return (uint32_t)(v < 0 ? 0 : v > 64 ? 64 : v);
+    }();
+    return g;
+}
+
 // VKBLAS_EPI_TMA=0 keeps the 2-byte epilogues on direct global stores.
 bool epi_tma_enabled() {
     static const bool on = [] {
@@ -1653,6 +1666,10 @@ cudaError_t launch_umma_gemm(const GemmProblem& p_in, int num_sms, int* d_status
     const uint32_t bm_tile = ks.bm_tile;
     prm.tiles_m = (p.M + bm_tile - 1) / bm_tile;
     prm.tiles_n = (p.N + BN - 1) / BN;
+    // Tile order.  Measured on B200 (one box), group of 8 -> all 16 M-blocks:
+    // HGEMM 4096^3 102.0 -> 100.3 us, but 3xTF32 SGEMM 4096^3 539.9 -> 543.7 us,
+    // and at 8192^3 (32 M-blocks) groups of 16 / 32 lost 2% / 10%.
+    prm.group_m = group_m() ? group_m() : (!is32 && prm.tiles_m <= 16u) ? 16u : 8u;
     prm.num_kb = (p.K + BK - 1) / BK;
     const uint64_t total = (uint64_t)prm.tiles_m * prm.tiles_n * p.batch;
     if (total >= (1ull << 31)) return cudaErrorNotSupported;
