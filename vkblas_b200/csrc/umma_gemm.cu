@@ -7,19 +7,26 @@
 // C = alpha*op(A)*op(B) + beta*C per batch entry, fp32 accumulation, fp32
 // epilogue with C unread when beta == 0, RNE store for 2-byte outputs.
 //
-// Structure (one CTA per SM, persistent over output tiles):
+// Structure (one CTA per SM, or one 2-CTA cluster per SM pair for 256-row
+// tiles, persistent over output tiles):
 //   warp 0      TMA producer: SWIZZLE_128B tiles of A and B into a STAGES-deep
-//               shared-memory ring (full/empty mbarrier pairs).  op(A)/op(B)
-//               are absorbed here: a K-major operand is loaded as rows of 128
-//               bytes of K, an MN-major one as 128-byte slabs of M (or N) per
-//               k-row, and the UMMA descriptors say which (no transpose pass,
-//               unlike the reference's transpose shaders, src/vkblas.c:970-1188).
+//               shared-memory ring (full/empty mbarrier pairs); a stage holds
+//               KBS consecutive k-blocks.  op(A)/op(B) are absorbed here: a
+//               K-major operand is loaded as rows of 128 bytes of K, an
+//               MN-major one as 128-byte slabs of M (or N) per k-row, and the
+//               UMMA descriptors say which (no transpose pass, unlike the
+//               reference's transpose shaders, src/vkblas.c:970-1188).
 //   warp 1      allocates TMEM (two accumulators, double-buffered across
 //               tiles) and issues tcgen05.mma from one thread; tcgen05.commit
 //               releases smem stages and hands finished accumulators over.
 //   warps 2-5   epilogue (2-9 for 3xTF32): tcgen05.ld (32 lanes x 32 columns
 //               per step) -> alpha/beta -> convert -> global, overlapping the
-//               next tile's main loop.
+//               next tile's main loop.  2-byte C goes through 32 x 64 boxes in
+//               shared memory and TMA stores (to peer copies of C as well).
+// 2-byte GEMMs are launched as programmatic dependents of the previous kernel
+// on the stream; every global access waits in griddepcontrol.wait first.
+// Long fp16/bf16 pair grids may run their last wave as 256 x 128 halves in a
+// second, dependent grid (the narrow tail, unit_coords).
 //
 // fp32 (3xTF32, after Ootomo & Yokota 2022, "Recovering single precision
 // accuracy from Tensor Cores while surpassing the FP32 theoretical peak
