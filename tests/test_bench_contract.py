@@ -66,3 +66,24 @@ def test_roofline_object_for_each_kernel_configuration():
     ffma_nom = bench._roofline("simt", 0, False, 1, 3.7, 3.7, peaks, "measured", None)
     assert abs(ffma_nom["peak"] - 148 * 128 * 2 * 1.965e-3) < 0.01
     json.dumps(wide)
+
+
+def test_fused_replication_roofline():
+    """The sharded secondary's roofline of the fused GEMM + P2P replication:
+    the slower of the rank's FLOPs at the bf16 burst rate and its NVLink bytes
+    at the measured peer-copy rate, against the measured time."""
+    sys.path.insert(0, ROOT)
+    import bench
+    # cfg5 on 4 GPUs: 64 GEMMs of 2048^3 per rank, 1.5 GiB sent per rank
+    r = {"with_p2p_epilogue": {"ms": 2.56}}
+    bench._fused_roofline(r, 64 * 2.0 * 2048 ** 3, 3 * 64 * 2048 * 2048 * 2, 1684.4)
+    rf = r["p2p_roofline"]
+    assert rf["bound"] == "nvlink"
+    assert abs(rf["link_ms"] - 3 * 64 * 2048 * 2048 * 2 / 770e9 * 1e3) < 1e-3
+    assert abs(rf["math_ms"] - 64 * 2.0 * 2048 ** 3 / 1684.4e12 * 1e3) < 1e-3
+    assert rf["target_ms"] == rf["link_ms"] and abs(rf["frac"] - rf["target_ms"] / 2.56) < 1e-3
+    # 16384^3 column shard on 2 GPUs: tensor-bound
+    r = {"with_p2p_epilogue": {"ms": 3.3}}
+    bench._fused_roofline(r, 2.0 * 16384 * 8192 * 16384, 8192 * 16384 * 2, 1684.4)
+    assert r["p2p_roofline"]["bound"] == "tensor"
+    assert 0 < r["p2p_roofline"]["frac"] <= 1
