@@ -522,17 +522,23 @@ __global__ void __launch_bounds__(Cfg<KIND, A_MN, B_MN, BN, STAGES, PAIR, KBS>::
                                 break;
                             }
                             tc_fence_after();
+                            // Descriptors of this stage's first k-block; the others
+                            // differ only in the start address field (bytes >> 4,
+                            // which stays inside its 14 bits below 256 KB).
+                            const uint32_t sA0 = sbase + stage * C_::STAGE_BYTES;
+                            const uint64_t ad0 = A_MN ? smem_desc_sw128(sA0, C_::SLAB, 1024)
+                                                      : smem_desc_sw128(sA0, 16, 1024);
+                            const uint64_t bd0 = B_MN ? smem_desc_sw128(sA0 + C_::A_PLANE, C_::SLAB, 1024)
+                                                      : smem_desc_sw128(sA0 + C_::A_PLANE, 16, 1024);
 #pragma unroll
                             for (uint32_t sub = 0; sub < (uint32_t)KBS; sub++) {
                                 if (sub >= nk) break;
-                                const uint32_t sA = sbase + stage * C_::STAGE_BYTES + sub * C_::KB_BYTES;
-                                const uint32_t sB = sA + C_::A_PLANE;
 #pragma unroll
                                 for (int j = 0; j < C_::KSTEPS; j++) {
-                                    const uint64_t ad = A_MN ? smem_desc_sw128(sA + j * C_::UK * ROW_BYTES, C_::SLAB, 1024)
-                                                             : smem_desc_sw128(sA + j * 32, 16, 1024);
-                                    const uint64_t bd = B_MN ? smem_desc_sw128(sB + j * C_::UK * ROW_BYTES, C_::SLAB, 1024)
-                                                             : smem_desc_sw128(sB + j * 32, 16, 1024);
+                                    constexpr uint32_t STEP = (A_MN ? C_::UK * ROW_BYTES : 32u) >> 4;
+                                    constexpr uint32_t STEPB = (B_MN ? C_::UK * ROW_BYTES : 32u) >> 4;
+                                    const uint64_t ad = ad0 + ((sub * C_::KB_BYTES) >> 4) + j * STEP;
+                                    const uint64_t bd = bd0 + ((sub * C_::KB_BYTES) >> 4) + j * STEPB;
                                     const uint32_t first = (si == 0 && sub == 0 && j == 0) ? 0u : 1u;
                                     if constexpr (PAIR) mma_f16_pair(d, ad, bd, C_::IDESC, first);
                                     else mma_f16(d, ad, bd, C_::IDESC, first);
