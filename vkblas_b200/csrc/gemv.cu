@@ -80,7 +80,8 @@ template <> struct Mma<__nv_bfloat16> {
 };
 
 // Weights: read once -> bypass L1, 256-byte L2 fetches (a step reads 256
-// contiguous bytes of each row).
+// contiguous bytes of each row).  Measured on B200 (4096 -> 14336, graph
+// replay): with a 128-byte or no fetch hint M = 1 took 23.2 us instead of 20.7.
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 v;
     asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
